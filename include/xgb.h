@@ -1,0 +1,187 @@
+/*
+ * xgb.h — C ABI of the xgen_b200 library (libxgb.so): the B200 (sm_100a)
+ * kernels behind xGen's sequence-parallel MiniMax-H3 attention hot path.
+ *
+ * Conventions shared by every entry point:
+ *   - Plain pointers to device memory, sizes and strides in ELEMENTS, and a
+ *     cudaStream_t passed as `void* stream` (NULL = legacy default stream).
+ *   - Return XGB_OK (0) or a negative status; never throw, never exit.
+ *   - No entry point allocates device memory. Kernels that need scratch
+ *     take a caller-provided workspace and export a *_workspace() sizing
+ *     function.
+ *   - Work is enqueued on `stream` only; calls are thread-compatible.
+ *   - dtype codes: XGB_BF16 or XGB_F16 for 16-bit floating inputs.
+ *
+ * Each declaration cites the reference (lightnateriver/xGen) function whose
+ * behaviour it reproduces, as path:line within that project.
+ */
+#ifndef XGB_H_
+#define XGB_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XGB_OK 0
+#define XGB_ERR_ARG (-1)       /* null pointer or out-of-range parameter */
+#define XGB_ERR_SHAPE (-2)     /* sizes the kernel does not support */
+#define XGB_ERR_STRIDE (-3)    /* strides the kernel does not support */
+#define XGB_ERR_ALIGN (-4)     /* pointer/stride alignment requirement not met */
+#define XGB_ERR_LAUNCH (-5)    /* CUDA reported an error for the launch */
+#define XGB_ERR_DEVICE (-6)    /* current device is not an sm_100 part */
+#define XGB_ERR_WORKSPACE (-7) /* workspace missing or smaller than required */
+
+#define XGB_BF16 0
+#define XGB_F16 1
+
+/* Library ABI version (major*100 + minor). */
+int xgb_version(void);
+
+/* Human-readable name of a status code (static string). */
+const char* xgb_status_string(int status);
+
+/* ---- Elementwise operators, bit-exact with the reference Triton kernels ---- */
+
+/* Rotate-half RoPE over the first `rotary` channels of contiguous bf16
+ * Q and K [batch, seq, heads, width]; cos/sin fp32 [seq, rotary], rounded to
+ * bf16 before use; every product rounded to bf16 as eager PyTorch does.
+ * Replaces _partial_rope / try_h3_partial_rope,
+ * x_base/x_base/operator/h3_partial_rope.py:9-47. */
+int xgb_partial_rope(const void* q, const void* k, const float* cos, const float* sin,
+                     void* q_out, void* k_out, int64_t batch, int64_t seq, int64_t heads,
+                     int64_t width, int64_t rotary, void* stream);
+
+/* Per-head RMSNorm of strided bf16 Q/K views [batch, seq, heads, width]
+ * (q_strides/k_strides = element strides of batch, seq, head; channel
+ * stride must be 1) times the bf16 weight, then optional rotate-half RoPE
+ * over `rotary` channels (rotary = 0 disables; cos/sin may then be NULL).
+ * Outputs are contiguous. Replaces _qk_rms / try_h3_qk_rms,
+ * x_base/x_base/operator/h3_qk_rms.py:9-84. */
+int xgb_qk_rms(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+               const void* q_weight, const void* k_weight, float q_eps, float k_eps,
+               const float* cos, const float* sin, int64_t rotary, void* q_out, void* k_out,
+               int64_t batch, int64_t seq, int64_t heads, int64_t width, void* stream);
+
+/* AdaLN indexed modulation (modulation = 1):
+ *     out = bf16(bf16(x * bf16(1 + table[idx])) + addend[idx])
+ * or gated residual (modulation = 0):
+ *     out = bf16(bf16(x * table[idx]) + addend)
+ * x/out contiguous bf16 [batch, seq, width]; table/addend rows strided by
+ * table_stride/addend_stride elements (addend contiguous like x when
+ * modulation = 0); indices int64 [seq].
+ * Replaces _indexed_affine / _apply,
+ * x_base/x_base/operator/h3_indexed_affine.py:9-49. */
+int xgb_indexed_affine(const void* x, const void* table, int64_t table_stride,
+                       const void* addend, int64_t addend_stride, const int64_t* indices,
+                       void* out, int64_t batch, int64_t seq, int64_t width, int modulation,
+                       void* stream);
+
+/* Gate-first packed SwiGLU: out[r, c] = bf16(bf16(g / (1 + exp(-g))) * v)
+ * with g = x[r, c], v = x[r, width + c]; x bf16 [rows, 2*width] contiguous.
+ * When amax_out is non-NULL it receives max |out| (NaN-propagating) — the
+ * caller zeroes it first (it is combined with atomic max).
+ * Replaces _swiglu / gate_first_swiglu,
+ * x_base/x_base/operator/h3_swiglu.py:15-41. */
+int xgb_swiglu(const void* x, void* out, int64_t rows, int64_t width, float* amax_out,
+               void* stream);
+
+/* ---- PHAA FP8 wire format (per-row e4m3 + fp32 scale) ---- */
+
+/* Encode `streams` (1 or 3) tensors into the PHAA byte wire. Each source is
+ * a 4-D view [peers, seq, batch, heads] of rows of `width` channels with
+ * element strides strides[4*s + 0..3] for source s (channel stride 1).
+ * Wire row = width e4m3 bytes + one fp32 scale, scale = max(amax/448,
+ * 1e-12); per peer the packet holds stream 0 rows, stream 1 rows, stream 2
+ * rows, then `peer_padding` zero bytes.
+ * When rotary > 0, streams 0 and 1 (Q, K) first get the rotate-half RoPE of
+ * xgb_partial_rope using cos/sin rows indexed by the `seq` coordinate —
+ * the two reference kernels fused, bit-exact with running them in turn.
+ * Replaces _encode, x_base/x_base/phaa/fp8_transport.py:26-63 (and the
+ * send side of fp8_all_to_all_many, :85-140). */
+int xgb_fp8_wire_encode(const void* const* sources, const int64_t* strides, int streams,
+                        int64_t peers, int64_t seq, int64_t batch, int64_t heads, int64_t width,
+                        int dtype, const float* cos, const float* sin, int64_t rotary,
+                        int64_t peer_padding, uint8_t* payload, void* stream);
+
+/* Decode the wire into `streams` contiguous outputs of rows*width elements
+ * (dest = e4m3 * scale, rounded to dtype). rows = total rows per stream.
+ * Replaces _decode, x_base/x_base/phaa/fp8_transport.py:66-78. */
+int xgb_fp8_wire_decode(const uint8_t* payload, void* const* dests, int streams, int64_t rows,
+                        int64_t peers, int64_t width, int64_t peer_padding, int dtype,
+                        void* stream);
+
+/* ---- FP8 Linear activation quantisation ---- */
+
+/* Bytes of workspace xgb_fp8_quantize_per_tensor needs for n elements. */
+int64_t xgb_fp8_quantize_per_tensor_workspace(int64_t n);
+
+/* Per-tensor dynamic e4m3: scale = max(amax(|x|)/448, FLT_MIN),
+ * out = e4m3(clamp(x/scale, +-448)); scale_out = one fp32 on the device.
+ * Replaces quantize_per_tensor (x_base/x_base/operator/h3_fp8.py:9-12) and
+ * quantize_activation + activation_abs_peak
+ * (h3_fp8_quant.py:18-25, h3_abs_peak.py:14-25). */
+int xgb_fp8_quantize_per_tensor(const void* x, int dtype, int64_t n, uint8_t* out,
+                                float* scale_out, void* workspace, int64_t workspace_bytes,
+                                void* stream);
+
+/* Per-token dynamic e4m3 (the per-token scaling of the B200 FP8 Linear):
+ * scales[r] = max(amax(|x[r,:]|)/448, FLT_MIN), out[r,c] = e4m3(x/scale).
+ * x rows strided by row_stride elements; out contiguous [rows, cols].
+ * Per-token counterpart of quantize_activation,
+ * x_base/x_base/operator/h3_fp8_quant.py:18-25. */
+int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, int64_t cols,
+                               int64_t row_stride, uint8_t* out, float* scales, void* stream);
+
+/* ---- Attention (tcgen05 / TMEM / TMA kernels) ---- */
+
+/* Bytes of workspace xgb_sage_prepare needs. */
+int64_t xgb_sage_prepare_workspace(int64_t batch, int64_t heads, int64_t seq);
+
+/* Sage quantisation of post-A2A Q/K/V views [batch, heads, seq, head_dim]
+ * (element strides b, h, s, d with d = 1; bf16 or fp16), head_dim = 128:
+ *   K <- K - mean over the seq real tokens (per head, per channel)
+ *   Q <- Q * sm_scale * log2(e); Q, K int8 per 64-token block (amax/127)
+ *   V e4m3 per channel: v_scale = max(amax/448, FLT_MIN)
+ * Outputs (16-byte aligned): q8/k8/v8 [batch*heads][S_pad][128] with
+ * S_pad = roundup(seq, 128) (rows >= seq zero), q_scale/k_scale
+ * [batch*heads][S_pad/64], v_scale [batch*heads][128].
+ * Replaces the quantisation inside `sageattn` as called at
+ * x_base/x_base/operator/attention.py:363-375 (SageAttention 2.2.0, not in
+ * the reference tree; algorithm per the SageAttention2 paper). */
+int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void* k,
+                     const int64_t* k_strides, const void* v, const int64_t* v_strides, int dtype,
+                     int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, float sm_scale,
+                     int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
+                     float* v_scale, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Non-causal attention over xgb_sage_prepare's outputs: INT8 Q.K^T
+ * (tcgen05 kind::i8), fp32 online softmax in the exp2 domain, e4m3 P.V
+ * (kind::f8f6f4), fp32 accumulation; writes bf16 out[b, h, s, :] at element
+ * strides out_strides (b, h, s, d = 1). error_flag (device int, may be
+ * NULL) receives a non-zero code if a bounded wait inside the kernel gave
+ * up. Replaces `sageattn(q, k, v, tensor_layout="HND", is_causal=False)`,
+ * x_base/x_base/operator/attention.py:363-375, via H3SageCUDA.__call__,
+ * x_base/x_base/operator/h3_sage_cuda.py:21-25. */
+int xgb_attention_sage(const int8_t* q8, const float* q_scale, const int8_t* k8,
+                       const float* k_scale, const uint8_t* v8, const float* v_scale,
+                       int64_t batch, int64_t heads, int64_t seq, void* out,
+                       const int64_t* out_strides, int* error_flag, void* stream);
+
+/* Non-causal BF16 attention (tcgen05 kind::f16, fp32 accumulation) reading
+ * q [b, h, seq_q, 128] and k/v [b, h, seq_kv, 128] views in place through
+ * TMA (strides in elements, multiples of 8, d stride 1), scale sm_scale.
+ * Replaces cuDNN SDPA in H3DenseCUDA.__call__,
+ * x_base/x_base/operator/h3_dense_cuda.py:11-15. */
+int xgb_attention_bf16(const void* q, const int64_t* q_strides, const void* k,
+                       const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_kv,
+                       float sm_scale, void* out, const int64_t* out_strides, int* error_flag,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XGB_H_ */

@@ -1,0 +1,110 @@
+"""tcgen05 attention kernels vs the CPU oracles.
+
+Tolerances (north-star parity targets): BF16 path cosine >= 0.9999 against
+fp32 SDPA with max-abs error <= 2e-2 (inputs N(0,1), outputs O(1)); Sage-FP8
+path cosine >= 0.999 against the quantised restatement."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oa
+
+pytestmark = pytest.mark.gpu
+
+
+def make_qkv(b, h, s, seed=0, k_bias=2.0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, h, s, 128, generator=g)
+    k = torch.randn(b, h, s, 128, generator=g) + k_bias * torch.randn(1, h, 1, 128, generator=g)
+    v = torch.randn(b, h, s, 128, generator=g)
+    return q.bfloat16(), k.bfloat16(), v.bfloat16()
+
+
+def to_np(t):
+    return t.float().cpu().numpy()
+
+
+def test_sage_prepare_vs_oracle(cuda_device):
+    from xgen_b200.attention import sage_prepare
+
+    q, k, v = make_qkv(1, 2, 300)
+    ws = sage_prepare(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device))
+    ref = oa.sage_quantize(to_np(q), to_np(k), to_np(v))
+    s = 300
+    nb = (s + 63) // 64
+    np.testing.assert_allclose(ws.q_scale.cpu().numpy()[:, :nb], ref["q_scale"].reshape(2, nb), rtol=1e-6)
+    np.testing.assert_allclose(ws.k_scale.cpu().numpy()[:, :nb], ref["k_scale"].reshape(2, nb), rtol=1e-5)
+    np.testing.assert_array_equal(ws.v_scale.cpu().numpy(), ref["v_scale"].reshape(2, 128))
+    q8 = ws.q8.cpu().numpy()[:, :s].reshape(1, 2, s, 128)
+    np.testing.assert_array_equal(q8, ref["q8"])
+    k8 = ws.k8.cpu().numpy()[:, :s].reshape(1, 2, s, 128).astype(np.int32)
+    dk = np.abs(k8 - ref["k8"].astype(np.int32))
+    assert dk.max() <= 1 and (dk > 0).mean() < 1e-3  # fp32 mean summation order
+    v8 = ws.v8.cpu().numpy()[:, :s].reshape(1, 2, s, 128)
+    np.testing.assert_array_equal(v8, ref["v8"])
+    # padding rows are zero
+    assert not ws.q8[:, s:].any() and not ws.k8[:, s:].any() and not ws.v8[:, s:].any()
+
+
+@pytest.mark.parametrize("b,h,s", [(1, 1, 128), (1, 2, 300), (2, 3, 1000), (1, 1, 4097)])
+def test_sage_attention_vs_oracle(cuda_device, b, h, s):
+    from xgen_b200.attention import kernel_errors, sage_attention
+
+    q, k, v = make_qkv(b, h, s, seed=s)
+    out = sage_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device))
+    torch.cuda.synchronize()
+    assert kernel_errors() == 0
+    got = to_np(out)
+    assert np.isfinite(got).all()
+    ref = oa.sage_attention(to_np(q), to_np(k), to_np(v))
+    assert oa.cosine(got, ref) >= 0.999
+    exact = oa.dense_attention(to_np(q), to_np(k), to_np(v))
+    assert oa.cosine(got, exact) >= 0.99
+
+
+@pytest.mark.parametrize("b,h,sq,skv", [(1, 1, 128, 128), (1, 2, 257, 257), (2, 3, 1000, 1000),
+                                        (1, 2, 300, 700)])
+def test_dense_attention_vs_sdpa(cuda_device, b, h, sq, skv):
+    from xgen_b200.attention import dense_attention, kernel_errors
+
+    g = torch.Generator().manual_seed(sq + skv)
+    q = torch.randn(b, h, sq, 128, generator=g).bfloat16()
+    k = torch.randn(b, h, skv, 128, generator=g).bfloat16()
+    v = torch.randn(b, h, skv, 128, generator=g).bfloat16()
+    out = dense_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device))
+    torch.cuda.synchronize()
+    assert kernel_errors() == 0
+    got = to_np(out)
+    ref = oa.dense_attention(to_np(q), to_np(k), to_np(v))
+    assert oa.cosine(got, ref) >= 0.9999
+    assert np.abs(got - ref).max() <= 2e-2
+
+
+def test_dense_attention_phaa_strided_views(cuda_device):
+    """q/k/v as views of a PHAA gather buffer [W_S, S, B, cs, D] ->
+    (B, cs, W_S*S, D), as test_bf16_cudnn_backend_with_phaa_strides does."""
+    from xgen_b200.attention import dense_attention
+
+    ws, s_loc, b, cs = 2, 129, 1, 2
+    bufs = [torch.randn(ws, s_loc, b, cs, 128, device=cuda_device).bfloat16() for _ in range(3)]
+    views = [x.flatten(0, 1).permute(1, 2, 0, 3).narrow(2, 0, ws * s_loc - 1) for x in bufs]
+    out = dense_attention(*views)
+    ref = torch.nn.functional.scaled_dot_product_attention(*(t.float() for t in views))
+    assert oa.cosine(to_np(out), to_np(ref)) >= 0.9999
+
+
+def test_backend_contract(cuda_device):
+    from xgen_b200.attention import H3AttentionBackendB200
+
+    q, k, v = (t.to(cuda_device) for t in make_qkv(1, 2, 513))
+    for precision in ("sage", "bf16"):
+        backend = H3AttentionBackendB200(precision)
+        out = backend(q, k, v, head_offset=0)
+        assert out.shape == q.shape and out.dtype == q.dtype
+        assert backend.calls == backend.kernel_calls == 1
+        mask = torch.ones(513, 513, dtype=torch.bool, device=cuda_device)
+        masked = backend(q, k, v, attn_mask=mask)
+        assert backend.calls == 2 and backend.kernel_calls == 1
+        assert masked.shape == q.shape

@@ -1,0 +1,166 @@
+"""CUDA elementwise/FP8 operators vs the reference's own outputs (golden
+fixtures) and vs the CPU oracle on larger seeded inputs — bit-exact unless a
+test states otherwise."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import elementwise as ew
+from oracle import fp8 as of
+from oracle.numerics import bf16_bits_from_f32, f32_from_bf16_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def dev_bf16(bits: np.ndarray, dev) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.uint16).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def host_bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def test_partial_rope_matches_reference(cuda_device):
+    from xgen_b200.ops import try_h3_partial_rope
+
+    g = golden("partial_rope")
+    with torch.no_grad():
+        for i in range(int(g["ncases"])):
+            b, s, h, w, r = g[f"c{i}_shape"]
+            q = dev_bf16(g[f"c{i}_q"], cuda_device).reshape(b, s, h, w)
+            k = dev_bf16(g[f"c{i}_k"], cuda_device).reshape(b, s, h, w)
+            cos = torch.from_numpy(g[f"c{i}_cos"]).to(cuda_device)
+            sin = torch.from_numpy(g[f"c{i}_sin"]).to(cuda_device)
+            qo, ko = try_h3_partial_rope(q, k, cos, sin)
+            assert np.array_equal(host_bits(qo).reshape(-1), g[f"c{i}_qo"].reshape(-1)), i
+            assert np.array_equal(host_bits(ko).reshape(-1), g[f"c{i}_ko"].reshape(-1)), i
+
+
+def test_partial_rope_large_vs_oracle(cuda_device):
+    from xgen_b200.ops import try_h3_partial_rope
+
+    gen = torch.Generator().manual_seed(5)
+    b, s, h, w, r = 1, 257, 24, 128, 96
+    q = torch.randn(b, s, h, w, generator=gen).bfloat16()
+    k = torch.randn(b, s, h, w, generator=gen).bfloat16()
+    theta = torch.arange(s, dtype=torch.float32)[:, None] * torch.rand(1, r, generator=gen)
+    cos, sin = torch.cos(theta), torch.sin(theta)
+    with torch.no_grad():
+        qo, ko = try_h3_partial_rope(q.to(cuda_device), k.to(cuda_device), cos.to(cuda_device),
+                                     sin.to(cuda_device))
+    eq, ek = ew.partial_rope(q.float().numpy(), k.float().numpy(), cos.numpy(), sin.numpy())
+    assert np.array_equal(host_bits(qo), bf16_bits_from_f32(eq))
+    assert np.array_equal(host_bits(ko), bf16_bits_from_f32(ek))
+
+
+def test_partial_rope_rejects_like_reference(cuda_device):
+    from xgen_b200.ops import try_h3_partial_rope
+
+    q = torch.randn(1, 4, 2, 128, device=cuda_device).bfloat16()
+    cos = torch.randn(4, 96, device=cuda_device)
+    with torch.no_grad():
+        assert try_h3_partial_rope(q.float(), q.float(), cos, cos) is None  # dtype
+        assert try_h3_partial_rope(q, q, cos[:, :95], cos[:, :95]) is None  # odd rotary
+        assert try_h3_partial_rope(q.cpu(), q.cpu(), cos.cpu(), cos.cpu()) is None  # not CUDA
+
+
+def test_qk_rms_matches_reference(cuda_device):
+    from xgen_b200.ops import try_h3_qk_rms
+
+    g = golden("qk_rms")
+    with torch.no_grad():
+        for i in range(int(g["ncases"])):
+            b, s, h, w, r = g[f"c{i}_shape"]
+            fused = dev_bf16(g[f"c{i}_fused"], cuda_device).reshape(b, s, 3 * h * w)
+            q, k, _ = fused.chunk(3, dim=-1)
+            q, k = q.unflatten(-1, (h, w)), k.unflatten(-1, (h, w))
+            eps = g[f"c{i}_eps"]
+            nq, nk = torch.nn.RMSNorm(w, eps=float(eps[0])), torch.nn.RMSNorm(w, eps=float(eps[1]))
+            nq.weight.data = dev_bf16(g[f"c{i}_qw"], cuda_device)
+            nk.weight.data = dev_bf16(g[f"c{i}_kw"], cuda_device)
+            rot = None
+            if r:
+                rot = (torch.from_numpy(g[f"c{i}_cos"]).to(cuda_device),
+                       torch.from_numpy(g[f"c{i}_sin"]).to(cuda_device))
+            qo, ko = try_h3_qk_rms(q, k, nq, nk, rot)
+            for ours, ref in ((qo, g[f"c{i}_qo"]), (ko, g[f"c{i}_ko"])):
+                # one bf16 ulp allowed where the fp32 sum-of-squares order
+                # (not part of the algorithm) moves a rounding boundary
+                d = np.abs(host_bits(ours).astype(np.int32).reshape(-1) - ref.astype(np.int32).reshape(-1))
+                assert d.max() <= 1 and (d > 0).mean() < 2e-3, (i, d.max(), (d > 0).mean())
+
+
+def test_indexed_affine_matches_reference(cuda_device):
+    from xgen_b200.ops import indexed_affine
+
+    g = golden("indexed_affine")
+    for i in range(int(g["ncases"])):
+        b, s, w, m = g[f"c{i}_shape"]
+        x = dev_bf16(g[f"c{i}_x"], cuda_device).reshape(b, s, w)
+        res = dev_bf16(g[f"c{i}_residual"], cuda_device).reshape(b, s, w)
+        tables = dev_bf16(g[f"c{i}_tables"], cuda_device).reshape(m, 6 * w)
+        shift, scale, gate, *_ = tables.chunk(6, dim=-1)
+        idx = torch.from_numpy(g[f"c{i}_idx"]).to(cuda_device)
+        mod = indexed_affine(x, scale, shift, idx, modulation=True)
+        gated = indexed_affine(x, gate, res, idx, modulation=False)
+        assert np.array_equal(host_bits(mod).reshape(-1), g[f"c{i}_mod"].reshape(-1)), i
+        assert np.array_equal(host_bits(gated).reshape(-1), g[f"c{i}_gate"].reshape(-1)), i
+        # and the reference's own eager formula (test_h3_indexed_affine.py:18-21)
+        eager = x * (1.0 + scale.index_select(0, idx)) + shift.index_select(0, idx)
+        assert torch.equal(mod, eager)
+
+
+def test_swiglu_matches_reference(cuda_device):
+    from xgen_b200.ops import gate_first_swiglu
+
+    g = golden("swiglu")
+    for i in range(int(g["ncases"])):
+        xb = g[f"c{i}_x"]
+        x = dev_bf16(xb, cuda_device).reshape(xb.shape)
+        y, amax = gate_first_swiglu(x, with_amax=True)
+        d = np.abs(host_bits(y).astype(np.int32).reshape(-1) - g[f"c{i}_y"].astype(np.int32).reshape(-1))
+        # CUDA expf vs IEEE exp can move a bf16 rounding boundary by one ulp
+        assert d.max() <= 1 and (d > 0).mean() < 1e-2, i
+        assert abs(amax.item() - float(g[f"c{i}_amax"][0])) <= 0.01 * float(g[f"c{i}_amax"][0])
+
+
+def test_fp8_quant_matches_reference(cuda_device):
+    from xgen_b200.ops import quantize_activation
+
+    g = golden("fp8_quant")
+    for i in range(int(g["ncases"])):
+        raw = g[f"c{i}_x"]
+        if int(g[f"c{i}_dtype"]) == 0:
+            x = dev_bf16(raw, cuda_device).reshape(raw.shape)
+        else:
+            x = torch.from_numpy(raw.view(np.float16)).to(cuda_device)
+        q, scale = quantize_activation(x)
+        assert scale.item() == float(g[f"c{i}_scale"][0]), i
+        assert np.array_equal(q.view(torch.uint8).cpu().numpy(), g[f"c{i}_q"]), i
+
+
+@pytest.mark.parametrize("shape", [(2048, 14336), (997, 5376)])
+def test_fp8_quant_large_matches_torch_reference(cuda_device, shape):
+    """The reference test's shapes (test_h3_cuda_precision_ops.py:49-58): our
+    kernel vs quantize_per_tensor written in torch (h3_fp8.py:9-12)."""
+    from xgen_b200.ops import quantize_activation
+
+    x = torch.randn(shape, device=cuda_device, dtype=torch.bfloat16)
+    for sample in (x, torch.zeros_like(x)):
+        maximum = torch.finfo(torch.float8_e4m3fn).max
+        scale = (sample.float().abs().amax() / maximum).clamp_min(torch.finfo(torch.float32).tiny)
+        expected = (sample.float() / scale).clamp(-maximum, maximum).to(torch.float8_e4m3fn)
+        actual, actual_scale = quantize_activation(sample)
+        assert torch.equal(actual_scale, scale)
+        assert torch.equal(actual.view(torch.uint8), expected.view(torch.uint8))
+
+
+def test_per_token_quant_vs_oracle(cuda_device):
+    from xgen_b200.ops import quantize_per_token
+
+    x = (torch.randn(333, 3072) * torch.rand(333, 1) * 10).bfloat16()
+    codes, scales = quantize_per_token(x.to(cuda_device))
+    rc, rs = of.quantize_per_token(x.float().numpy())
+    assert np.array_equal(scales.cpu().numpy(), rs)
+    assert np.array_equal(codes.view(torch.uint8).cpu().numpy(), rc)

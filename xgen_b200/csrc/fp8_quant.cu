@@ -1,0 +1,200 @@
+// Dynamic e4m3 activation quantisation for the FP8 Linear.
+//
+// Per-tensor (the reference's scheme, x_base/x_base/operator/h3_fp8.py:9-12,
+// h3_fp8_quant.py:9-25, h3_abs_peak.py:14-25):
+//   peaks[b] = max |x| over block b            (NaN-propagating)
+//   scale    = max(max(peaks) / 448, FLT_MIN)
+//   out      = e4m3(clamp(x / scale, +-448))   (IEEE division, RNE)
+// The max is order-independent, so the result is bit-exact with the
+// reference whatever the block split; the per-block peaks live in a
+// caller-provided workspace, as the reference's `peaks` tensor does.
+//
+// Per-token (the B200 FP8 Linear's activation scheme): the same formula per
+// row, computed by one warp per row.
+#include <cfloat>
+
+#include "xgb_common.cuh"
+
+namespace xgb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int64_t kPeakBlock = 8192;  // elements per peak, as the reference
+
+template <typename T>
+__device__ __forceinline__ float to_float(T v);
+template <>
+__device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_float<__half>(__half v) { return __half2float(v); }
+
+__device__ __forceinline__ int abs_bits(float v) { return __float_as_int(fabsf(v)); }
+
+// Block peaks: |x| bit images compared as integers (NaN sorts above +inf).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) abs_peak_kernel(const T* __restrict__ x, int64_t n,
+                                                            int* __restrict__ peaks) {
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kPeakBlock;
+  const int64_t end = min(base + kPeakBlock, n);
+  int m = 0;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (end - base) % 8 == 0;
+  if (vec) {
+    for (int64_t i = base + threadIdx.x * 8; i < end; i += kThreads * 8) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + i));
+      const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = max(m, abs_bits(to_float<T>(v[j])));
+    }
+  } else {
+    for (int64_t i = base + threadIdx.x; i < end; i += kThreads) m = max(m, abs_bits(to_float<T>(x[i])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ int warp_peak[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_peak[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int r = 0;
+    for (int w = 0; w < kThreads / 32; ++w) r = max(r, warp_peak[w]);
+    peaks[blockIdx.x] = r;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) peak_to_scale_kernel(const int* __restrict__ peaks,
+                                                                 int64_t blocks,
+                                                                 float* __restrict__ scale) {
+  int m = 0;
+  for (int64_t i = threadIdx.x; i < blocks; i += kThreads) m = max(m, peaks[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ int warp_peak[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_peak[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int r = 0;
+    for (int w = 0; w < kThreads / 32; ++w) r = max(r, warp_peak[w]);
+    const float s = __fdiv_rn(__int_as_float(r), 448.0f);
+    *scale = isnan(s) ? s : fmaxf(s, FLT_MIN);  // clamp_min keeps NaN
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) pack_kernel(const T* __restrict__ x, int64_t n,
+                                                        const float* __restrict__ scale_ptr,
+                                                        uint8_t* __restrict__ out) {
+  const float scale = __ldg(scale_ptr);
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 8;
+  if (i >= n) return;
+  if (i + 8 <= n && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 7u) == 0) {
+    uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + i));
+    const T* v = reinterpret_cast<const T*>(&raw);
+    uint8_t b[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      b[j] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(v[j]), scale), -448.f), 448.f));
+    *reinterpret_cast<uint2*>(out + i) = *reinterpret_cast<uint2*>(b);
+  } else {
+    for (int64_t j = i; j < min(i + 8, n); ++j)
+      out[j] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(x[j]), scale), -448.f), 448.f));
+  }
+}
+
+// One warp per row: amax, scale, pack.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) per_token_kernel(const T* __restrict__ x, int64_t rows,
+                                                             int64_t cols, int64_t row_stride,
+                                                             uint8_t* __restrict__ out,
+                                                             float* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* src = x + row * row_stride;
+  uint8_t* dst = out + row * cols;
+  const bool vec = cols % 8 == 0 && row_stride % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  int m = 0;
+  if (vec) {
+    for (int64_t c = lane * 8; c < cols; c += 256) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(src + c));
+      const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = max(m, abs_bits(to_float<T>(v[j])));
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) m = max(m, abs_bits(to_float<T>(src[c])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float amax_scale = __fdiv_rn(__int_as_float(m), 448.0f);
+  const float scale = isnan(amax_scale) ? amax_scale : fmaxf(amax_scale, FLT_MIN);
+  if (lane == 0) scales[row] = scale;
+  if (vec) {
+    for (int64_t c = lane * 8; c < cols; c += 256) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(src + c));
+      const T* v = reinterpret_cast<const T*>(&raw);
+      uint8_t b[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        b[j] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(v[j]), scale), -448.f), 448.f));
+      *reinterpret_cast<uint2*>(dst + c) = *reinterpret_cast<uint2*>(b);
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32)
+      dst[c] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(src[c]), scale), -448.f), 448.f));
+  }
+}
+
+}  // namespace
+}  // namespace xgb
+
+using namespace xgb;
+
+XGB_API int64_t xgb_fp8_quantize_per_tensor_workspace(int64_t n) {
+  if (n <= 0) return 0;
+  return cdiv(n, kPeakBlock) * static_cast<int64_t>(sizeof(int));
+}
+
+XGB_API int xgb_fp8_quantize_per_tensor(const void* x, int dtype, int64_t n, uint8_t* out,
+                                        float* scale_out, void* workspace,
+                                        int64_t workspace_bytes, void* stream) {
+  if (!x || !out || !scale_out) return XGB_ERR_ARG;
+  if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
+  if (n <= 0) return XGB_ERR_SHAPE;
+  const int64_t blocks = cdiv(n, kPeakBlock);
+  if (!workspace || workspace_bytes < xgb_fp8_quantize_per_tensor_workspace(n))
+    return XGB_ERR_WORKSPACE;
+  int* peaks = static_cast<int*>(workspace);
+  cudaStream_t st = as_stream(stream);
+  const unsigned pack_grid = static_cast<unsigned>(cdiv(cdiv(n, 8), kThreads));
+  if (dtype == XGB_BF16) {
+    auto xb = static_cast<const __nv_bfloat16*>(x);
+    abs_peak_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(xb, n, peaks);
+    peak_to_scale_kernel<<<1, kThreads, 0, st>>>(peaks, blocks, scale_out);
+    pack_kernel<<<pack_grid, kThreads, 0, st>>>(xb, n, scale_out, out);
+  } else {
+    auto xh = static_cast<const __half*>(x);
+    abs_peak_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(xh, n, peaks);
+    peak_to_scale_kernel<<<1, kThreads, 0, st>>>(peaks, blocks, scale_out);
+    pack_kernel<<<pack_grid, kThreads, 0, st>>>(xh, n, scale_out, out);
+  }
+  return launch_status();
+}
+
+XGB_API int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, int64_t cols,
+                                       int64_t row_stride, uint8_t* out, float* scales,
+                                       void* stream) {
+  if (!x || !out || !scales) return XGB_ERR_ARG;
+  if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
+  if (rows < 0 || cols <= 0 || row_stride < cols) return XGB_ERR_SHAPE;
+  if (rows == 0) return XGB_OK;
+  const unsigned grid = static_cast<unsigned>(cdiv(rows, kThreads / 32));
+  cudaStream_t st = as_stream(stream);
+  if (dtype == XGB_BF16)
+    per_token_kernel<<<grid, kThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, cols,
+                                                 row_stride, out, scales);
+  else
+    per_token_kernel<<<grid, kThreads, 0, st>>>(static_cast<const __half*>(x), rows, cols,
+                                                 row_stride, out, scales);
+  return launch_status();
+}

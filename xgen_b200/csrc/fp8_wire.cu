@@ -1,0 +1,252 @@
+// PHAA FP8 wire codec: one byte A2A payload carrying per-row e4m3 values and
+// an fp32 row scale, optionally with the pre-A2A rotate-half RoPE fused in.
+//
+// Wire layout (x_base/x_base/phaa/fp8_transport.py:26-63, :103-112):
+//   per peer p: [stream0 rows][stream1 rows][stream2 rows][peer_padding zeros]
+//   row:        width e4m3 bytes, then the fp32 scale
+//   scale       = max(max|x| / 448, 1e-12); byte = e4m3(clamp(x/scale, +-448))
+// The division is IEEE (__fdiv_rn), matching the reference algorithm as the
+// Triton interpreter evaluates it.
+//
+// Work split: a group of G = next_pow2(width/8) lanes owns one row, each lane
+// 8 channels; 32/G rows per warp, so width=128 uses full warps (2 rows each).
+#include "xgb_common.cuh"
+
+namespace xgb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxStreams = 3;
+
+struct EncodeArgs {
+  const void* src[kMaxStreams];
+  int64_t st[kMaxStreams][4];  // element strides: peer, seq, batch, head
+  int64_t peers, seq, batch, heads, width, rows, peer_rows, peer_padding;
+  int streams;
+  const float* cos;
+  const float* sin;
+  int64_t rotary;
+  uint8_t* payload;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+template <typename T, bool kVec>
+__device__ __forceinline__ void load_row8(const T* p, int valid, float (&out)[8]) {
+  if (kVec && valid == 8) {
+    uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+    const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = to_f<T>(v[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = i < valid ? to_f<T>(p[i]) : 0.f;
+  }
+}
+
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int group) {
+  const int slot = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & (group - 1);             // lane within the row group
+  const int rows_per_warp = 32 / group;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5)) *
+                          rows_per_warp + lane / group;
+  const bool live = row < a.rows;
+  const int64_t r = live ? row : 0;
+  const int64_t head = r % a.heads;
+  const int64_t bat = (r / a.heads) % a.batch;
+  const int64_t s = (r / (a.heads * a.batch)) % a.seq;
+  const int64_t peer = r / a.peer_rows;
+  const T* src = static_cast<const T*>(a.src[slot]) + peer * a.st[slot][0] + s * a.st[slot][1] +
+                 bat * a.st[slot][2] + head * a.st[slot][3];
+  const int c0 = sub * 8;
+  const int valid = live ? max(0, min(8, static_cast<int>(a.width) - c0)) : 0;
+
+  float x[8];
+  load_row8<T, kVec>(src + c0, valid, x);
+  if (a.rotary > 0 && slot < 2 && c0 < a.rotary) {
+    // Fused pre-A2A RoPE (h3_partial_rope.py:9-29): bf16 result, then encode.
+    const int64_t half = a.rotary / 2;
+    float p[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t c = c0 + i;
+      if (i < valid && c < a.rotary) {
+        const bool first = c < half;
+        p[i] = to_f<T>(src[first ? c + half : c - half]);
+        const float cb = bf16_round(a.cos[s * a.rotary + c]);
+        const float sb = bf16_round(a.sin[s * a.rotary + c]);
+        const float left = bf16_round(__fmul_rn(x[i], cb));
+        const float right = bf16_round(__fmul_rn(first ? -p[i] : p[i], sb));
+        x[i] = to_f<T>(from_f<T>(__fadd_rn(left, right)));
+      }
+    }
+  }
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(x[i]));
+  for (int o = group / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float scale = fmaxf(__fdiv_rn(m, 448.0f), 1.0e-12f);
+  if (!live) return;
+
+  const int64_t wire_row = row + (peer * (a.streams - 1) + slot) * a.peer_rows;
+  const int64_t offset = wire_row * (a.width + 4) + peer * a.peer_padding;
+  uint8_t* dst = a.payload + offset;
+  uint8_t b[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float q = fminf(fmaxf(__fdiv_rn(x[i], scale), -448.0f), 448.0f);
+    b[i] = f32_to_e4m3(q);
+  }
+  if (valid == 8) {
+    // Rows start at 4-byte multiples (width % 4 == 0), so two u32 stores.
+    reinterpret_cast<uint32_t*>(dst + c0)[0] = *reinterpret_cast<uint32_t*>(b);
+    reinterpret_cast<uint32_t*>(dst + c0)[1] = *reinterpret_cast<uint32_t*>(b + 4);
+  } else {
+    for (int i = 0; i < valid; ++i) dst[c0 + i] = b[i];
+  }
+  if (sub == 0) *reinterpret_cast<float*>(dst + a.width) = scale;
+  if (a.peer_padding && sub == 0 && slot == 0 && row % a.peer_rows == 0) {
+    const int64_t packet = a.peer_rows * a.streams * (a.width + 4);
+    uint8_t* tail = a.payload + peer * (packet + a.peer_padding) + packet;
+    for (int64_t i = 0; i < a.peer_padding; ++i) tail[i] = 0;
+  }
+}
+
+struct DecodeArgs {
+  const uint8_t* payload;
+  void* dst[kMaxStreams];
+  int64_t width, rows, peer_rows, peer_padding;
+  int streams;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) wire_decode_kernel(DecodeArgs a, int group) {
+  const int slot = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & (group - 1);
+  const int rows_per_warp = 32 / group;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5)) *
+                          rows_per_warp + lane / group;
+  if (row >= a.rows) return;
+  const int c0 = sub * 8;
+  const int valid = max(0, min(8, static_cast<int>(a.width) - c0));
+  if (valid == 0) return;
+  const int64_t peer = row / a.peer_rows;
+  const int64_t wire_row = row + (peer * (a.streams - 1) + slot) * a.peer_rows;
+  const uint8_t* src = a.payload + wire_row * (a.width + 4) + peer * a.peer_padding;
+  const float scale = __ldg(reinterpret_cast<const float*>(src + a.width));
+  T* dst = static_cast<T*>(a.dst[slot]) + row * a.width + c0;
+  uint8_t b[8];
+  if (valid == 8) {
+    *reinterpret_cast<uint32_t*>(b) = __ldg(reinterpret_cast<const uint32_t*>(src + c0));
+    *reinterpret_cast<uint32_t*>(b + 4) = __ldg(reinterpret_cast<const uint32_t*>(src + c0 + 4));
+  } else {
+    for (int i = 0; i < valid; ++i) b[i] = src[c0 + i];
+  }
+  T out[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = from_f<T>(__fmul_rn(e4m3_to_f32(b[i]), scale));
+  if (valid == 8 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(out);
+  } else {
+    for (int i = 0; i < valid; ++i) dst[i] = out[i];
+  }
+}
+
+int group_for(int64_t width) {
+  int lanes = static_cast<int>((width + 7) / 8);
+  int g = 1;
+  while (g < lanes) g <<= 1;
+  return g;
+}
+
+}  // namespace
+}  // namespace xgb
+
+using namespace xgb;
+
+XGB_API int xgb_fp8_wire_encode(const void* const* sources, const int64_t* strides, int streams,
+                                int64_t peers, int64_t seq, int64_t batch, int64_t heads,
+                                int64_t width, int dtype, const float* cos, const float* sin,
+                                int64_t rotary, int64_t peer_padding, uint8_t* payload,
+                                void* stream) {
+  if (!sources || !strides || !payload) return XGB_ERR_ARG;
+  if (streams != 1 && streams != 3) return XGB_ERR_ARG;
+  if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
+  if (peers <= 0 || seq < 0 || batch < 0 || heads < 0) return XGB_ERR_SHAPE;
+  if (width <= 0 || width % 4 || width > 256) return XGB_ERR_SHAPE;
+  if (peer_padding < 0 || peer_padding >= 16 || peer_padding % 4) return XGB_ERR_ARG;
+  if (rotary < 0 || rotary % 2 || rotary > width) return XGB_ERR_SHAPE;
+  if (rotary > 0 && (!cos || !sin || dtype != XGB_BF16)) return XGB_ERR_ARG;
+  EncodeArgs a{};
+  a.rows = peers * seq * batch * heads;
+  if (a.rows == 0) return XGB_OK;
+  bool vec = true;
+  for (int s = 0; s < streams; ++s) {
+    if (!sources[s]) return XGB_ERR_ARG;
+    a.src[s] = sources[s];
+    for (int d = 0; d < 4; ++d) {
+      a.st[s][d] = strides[4 * s + d];
+      if (a.st[s][d] % 8) vec = false;
+    }
+    if (reinterpret_cast<uintptr_t>(sources[s]) & 15u) vec = false;
+  }
+  if (width % 8) vec = false;
+  a.peers = peers; a.seq = seq; a.batch = batch; a.heads = heads; a.width = width;
+  a.peer_rows = a.rows / peers;
+  a.peer_padding = peer_padding; a.streams = streams;
+  a.cos = cos; a.sin = sin; a.rotary = rotary; a.payload = payload;
+  const int group = group_for(width);
+  const int64_t rows_per_block = (kThreads / 32) * (32 / group);
+  dim3 grid(static_cast<unsigned>(cdiv(a.rows, rows_per_block)), streams);
+  cudaStream_t st = as_stream(stream);
+  if (dtype == XGB_BF16) {
+    if (vec) wire_encode_kernel<__nv_bfloat16, true><<<grid, kThreads, 0, st>>>(a, group);
+    else wire_encode_kernel<__nv_bfloat16, false><<<grid, kThreads, 0, st>>>(a, group);
+  } else {
+    if (vec) wire_encode_kernel<__half, true><<<grid, kThreads, 0, st>>>(a, group);
+    else wire_encode_kernel<__half, false><<<grid, kThreads, 0, st>>>(a, group);
+  }
+  return launch_status();
+}
+
+XGB_API int xgb_fp8_wire_decode(const uint8_t* payload, void* const* dests, int streams,
+                                int64_t rows, int64_t peers, int64_t width, int64_t peer_padding,
+                                int dtype, void* stream) {
+  if (!payload || !dests) return XGB_ERR_ARG;
+  if (streams != 1 && streams != 3) return XGB_ERR_ARG;
+  if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
+  if (rows < 0 || peers <= 0 || rows % peers) return XGB_ERR_SHAPE;
+  if (width <= 0 || width % 4 || width > 256) return XGB_ERR_SHAPE;
+  if (peer_padding < 0 || peer_padding >= 16 || peer_padding % 4) return XGB_ERR_ARG;
+  if (rows == 0) return XGB_OK;
+  DecodeArgs a{};
+  a.payload = payload;
+  for (int s = 0; s < streams; ++s) {
+    if (!dests[s]) return XGB_ERR_ARG;
+    a.dst[s] = dests[s];
+  }
+  a.width = width; a.rows = rows; a.peer_rows = rows / peers;
+  a.peer_padding = peer_padding; a.streams = streams;
+  const int group = group_for(width);
+  const int64_t rows_per_block = (kThreads / 32) * (32 / group);
+  dim3 grid(static_cast<unsigned>(cdiv(rows, rows_per_block)), streams);
+  cudaStream_t st = as_stream(stream);
+  if (dtype == XGB_BF16) wire_decode_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(a, group);
+  else wire_decode_kernel<__half><<<grid, kThreads, 0, st>>>(a, group);
+  return launch_status();
+}
