@@ -1,0 +1,424 @@
+"""Benchmark: Ulysses-SP H3 self-attention at the 768P-5s shape on B200.
+
+One step = one SP self-attention layer of the MiniMax-H3 DiT (BASELINE
+config 2/3 shape: 31x48x84 video + 512 text + 1,250 audio = 126,754 tokens,
+24 heads x 128): RoPE on Q/K, the seq->head redistribution, Sage-FP8 (or
+BF16) attention on tcgen05, and the head->seq return, per rank on
+S_loc = S_pad / N tokens. At N > 1 the redistribution is PHAA over NCCL with
+the FP8 wire (RoPE fused into the encode, attention epilogue writing the
+return send buffer). Inputs are synthetic (seeded N(0,1) Q/V, K with a
+per-head channel bias of std 2), resident in HBM before timing and larger
+than L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--precision sage|bf16]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference   # the reference's CPU attention path
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "SP attention TFLOP/s/GPU and DiT block ms at 768P-5s, 1/2/4/8 B200"
+GRID = (31, 48, 84)
+TEXT, AUDIO = 512, 1250
+HEADS, HEAD_DIM = 24, 128
+SEQ = GRID[0] * GRID[1] * GRID[2] + TEXT + AUDIO  # 126,754
+FLOPS_PER_LAYER = 4.0 * SEQ * SEQ * HEAD_DIM * HEADS  # non-causal QK^T + PV
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--precision", choices=("sage", "bf16"), default="sage")
+    ap.add_argument("--phaa-num", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ helpers
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].isdigit():
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                "samples": len(rows), "reasons": reasons}
+
+
+def cpu_attention_sample(seconds: float, threads: int | None = None):
+    """The reference's CPU attention path (fp32 SDPA, x_base/x_base/operator/
+    attention.py:29-34) on one head of the full 126,754-token sequence with a
+    sample of query rows, sized to ~`seconds` of work; returns TFLOP/s."""
+    import torch
+
+    from oracle.attention import dense_attention  # the oracle port of that path
+
+    if threads:
+        torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    k = torch.randn(1, 1, SEQ, HEAD_DIM, generator=g).numpy()
+    v = torch.randn(1, 1, SEQ, HEAD_DIM, generator=g).numpy()
+    rows = 256
+    total_flops, total_time = 0.0, 0.0
+    while total_time < seconds:
+        q = torch.randn(1, 1, rows, HEAD_DIM, generator=g).numpy()
+        t0 = time.perf_counter()
+        dense_attention(q, k, v)
+        dt = time.perf_counter() - t0
+        total_flops += 4.0 * rows * SEQ * HEAD_DIM
+        total_time += dt
+        if dt < seconds / 8:
+            rows *= 2
+    return total_flops / total_time / 1e12, total_flops, total_time, torch.get_num_threads()
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import torch
+
+    threads = os.cpu_count() or 1
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        tflops, flops, secs, used = cpu_attention_sample(max(2.0, args.cpu_seconds / 4), threads)
+        if i >= args.warmup:
+            per_step.append((tflops, flops, secs))
+    value = statistics.median(t for t, _, _ in per_step)
+    sample = (f"fp32 SDPA on CPU: 1 head, growing query-row samples x {SEQ} keys, "
+              f"~{per_step[0][2]:.1f}s per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": FLOPS_PER_LAYER / (value * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(world, "reference-cpu"),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": used, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(world, precision):
+    return {"workload": "h3-sp-self-attention-768p5s", "seq_real": SEQ, "grid": list(GRID),
+            "text_tokens": TEXT, "audio_tokens": AUDIO, "heads": HEADS, "head_dim": HEAD_DIM,
+            "sp": world, "precision": precision, "parallelism": f"sp{world}",
+            "l2": "inputs larger than L2 (3 x S_loc x 3072 bf16 per rank)"}
+
+
+# ------------------------------------------------------------------ B200 arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from xgen_b200 import _lib
+    from xgen_b200.attention import H3AttentionBackendB200, kernel_errors
+    from xgen_b200.h3.rope import rope_3d
+    from xgen_b200.h3.sp_attention import sp_self_attention
+    from xgen_b200.sp.padding import get_pad_manager
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        group = dist.group.WORLD
+    _lib.lib()
+
+    # Workload: pad the packed sequence to a multiple of 16*SP.
+    s_pad = -(-SEQ // (16 * world)) * (16 * world)
+    s_loc = s_pad // world
+    get_pad_manager()._pads["mmh3_seq"] = s_pad - SEQ
+    cos_full, sin_full = rope_3d(GRID, TEXT + AUDIO)
+    pad_rows = torch.zeros(s_pad - SEQ, HEAD_DIM)
+    cos_full = torch.cat([cos_full, pad_rows + 1.0])
+    sin_full = torch.cat([sin_full, pad_rows])
+    cos = cos_full[rank * s_loc:(rank + 1) * s_loc].contiguous().to(dev)
+    sin = sin_full[rank * s_loc:(rank + 1) * s_loc].contiguous().to(dev)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    width = HEADS * HEAD_DIM
+    q = torch.randn(1, s_loc, width, device=dev, generator=g).bfloat16()
+    k_bias = torch.randn(1, 1, width, device=dev, generator=torch.Generator(device=dev).manual_seed(7)) * 2.0
+    k = (torch.randn(1, s_loc, width, device=dev, generator=g) + k_bias).bfloat16()
+    v = torch.randn(1, s_loc, width, device=dev, generator=g).bfloat16()
+    if world > 1 and rank == world - 1 and s_pad > SEQ:
+        for t in (q, k, v):  # the tail padding rows are zeros, as split_sequence makes them
+            t[:, s_loc - (s_pad - SEQ):].zero_()
+
+    backend = H3AttentionBackendB200(args.precision)
+    comm_stream = torch.cuda.Stream(device=dev) if world > 1 else None
+    fp8_wire = args.precision == "sage"
+
+    def step(qq, kk, vv):
+        return sp_self_attention(qq, kk, vv, (cos, sin), backend=backend, heads=HEADS,
+                                 head_dim=HEAD_DIM, sp_group=group, sp_size=world,
+                                 phaa_num=min(args.phaa_num, HEADS // world),
+                                 fp8_transport=fp8_wire, comm_stream=comm_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    for _ in range(args.warmup):
+        out = step(q, k, v)
+    barrier()
+    launches_before = backend.kernel_calls
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            out = step(q, k, v)
+        end.record()
+        barrier()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    attn_calls = (backend.kernel_calls - launches_before) // args.steps
+    assert kernel_errors(dev) == 0, "a tcgen05 kernel reported a timed-out wait"
+    value = FLOPS_PER_LAYER / (ms * 1e-3) / 1e12  # aggregate over all ranks
+
+    # ---- dominant kernel alone: the attention kernel on prepared inputs
+    roof = attention_roofline(args.precision, world, dev, s_pad)
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = end_to_end(step, q, k, v, args, world, dev, barrier, max_over_ranks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tflops, flops, secs, used = cpu_attention_sample(args.cpu_seconds)
+        cpu = {"value": tflops, "unit": "TFLOP/s", "cores": used, "kind": "port",
+               "sample": f"fp32 SDPA (oracle port of attention.py:29-34) on 1 head: "
+                         f"{flops / 4 / SEQ / HEAD_DIM:.0f} query rows x {SEQ} keys in {secs:.1f}s"}
+
+    kernels_per_layer = kernels_per_step(args.precision, world, min(args.phaa_num, HEADS // world))
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8/e4m3 (fp32 accumulate)" if args.precision == "sage" else "bf16",
+        "data": "synthetic", "config": workload_config(world, args.precision),
+        "per_gpu_tflops": value / world, "attention_calls_per_step": attn_calls,
+        "gpu_launches": kernels_per_layer * args.steps,
+        "clocks": clocks.summary(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del out
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def kernels_per_step(precision, world, phaa):
+    """Our kernel launches per layer: SP=1: RoPE + (Sage: 3 prepare + 1 attention).
+    SP>1 per PHAA chunk: QKV encode, decode, (Sage: 3 prepare) + attention,
+    return encode, decode."""
+    attn = 4 if precision == "sage" else 1
+    if world == 1:
+        return 1 + attn
+    per_chunk = attn + (4 if precision == "sage" else 0)
+    return phaa * per_chunk + (1 if precision != "sage" else 0)
+
+
+def attention_roofline(precision, world, dev, s_pad):
+    """Time the attention kernel alone (CUDA events on its stream) on this
+    rank's head shard of the full sequence; achieved = algorithmic FLOPs per
+    launch / mean launch time; peak = in-run cuBLAS FP8 (or BF16) GEMM."""
+    import torch
+
+    from xgen_b200.attention import SageWorkspace, dense_attention, sage_attention_prepared, sage_prepare
+
+    heads = HEADS // world
+    g = torch.Generator(device=dev).manual_seed(99)
+    q = torch.randn(1, heads, SEQ, HEAD_DIM, device=dev, generator=g).bfloat16()
+    k = torch.randn(1, heads, SEQ, HEAD_DIM, device=dev, generator=g).bfloat16()
+    v = torch.randn(1, heads, SEQ, HEAD_DIM, device=dev, generator=g).bfloat16()
+    out = torch.empty_like(q)
+    if precision == "sage":
+        ws = sage_prepare(q, k, v)
+        run = lambda: sage_attention_prepared(ws, out)  # noqa: E731
+    else:
+        run = lambda: dense_attention(q, k, v, out=out)  # noqa: E731
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    reps = 5
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / reps
+    flops = 4.0 * SEQ * SEQ * HEAD_DIM * heads
+    achieved = flops / (ms * 1e-3) / 1e12
+    peak, peak_src = gemm_peak(dev, precision)
+    traffic = profile_traffic(precision, heads)
+    return {"bound": "tensor", "kernel": f"attention_kernel<{'sage' if precision == 'sage' else 'bf16'}>",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_source": peak_src, "kernel_ms": ms, "flops_per_launch": flops,
+            "traffic": traffic}
+
+
+def gemm_peak(dev, precision):
+    """Dense tensor peak measured in-run: torch._scaled_mm e4m3 8192^3 (cuBLASLt)
+    for the Sage kernel, else MEASURED_PEAKS.json's bf16 burst figure."""
+    import torch
+
+    if precision != "sage":
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        if "bf16_tflops" in peaks:
+            return peaks["bf16_tflops"], "MEASURED_PEAKS.json bf16_tflops (burst, cuBLAS)"
+        return 1590.0, "fallback 1.59 PFLOP/s bf16"
+    n = 8192
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=dev)
+    for _ in range(3):
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12, "in-run cuBLASLt e4m3 GEMM 8192^3, best of 10 (burst)"
+
+
+def profile_traffic(precision, heads):
+    """DRAM bytes per launch from the committed ncu summary, scaled to this
+    launch's heads (traffic grows in proportion to heads at fixed S)."""
+    path = ROOT / "profiles" / f"attention_{precision}_traffic.json"
+    if not path.exists():
+        return None
+    rec = json.loads(path.read_text())
+    return rec["dram_bytes_per_head"] * heads
+
+
+def end_to_end(step, q, k, v, args, world, dev, barrier, max_over_ranks):
+    """Same layer through the public API with pinned host buffers: H2D of
+    the step's Q/K/V shard and D2H of its output inside the timed region."""
+    import torch
+
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    steps = max(2, min(args.steps, 5))
+    dq, dk, dv = (torch.empty_like(t) for t in (q, k, v))
+
+    def one():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        out = step(dq, dk, dv)
+        hout.copy_(out, non_blocking=True)
+
+    one()
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        one()
+    e.record()
+    barrier()
+    ms = max_over_ranks(s.elapsed_time(e) / steps)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = hout.numel() * hout.element_size()
+    return {"value": FLOPS_PER_LAYER / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps}
+
+
+if __name__ == "__main__":
+    main()

@@ -73,11 +73,20 @@ def peer_padding(peer_rows: int, streams: int, width: int) -> int:
     return (-(peer_rows * streams * (width + 4))) % 16
 
 
-def quantize_per_tensor(x: np.ndarray):
-    """scale = max(amax/448, FLT_MIN); codes = e4m3(clamp(x/scale, +-448))."""
+def quantize_per_tensor(x: np.ndarray, scalar_div: str = "cuda"):
+    """scale = max(amax/448, FLT_MIN); codes = e4m3(clamp(x/scale, +-448)).
+
+    `amax / 448.0` is a torch tensor-by-Python-scalar division. On CUDA
+    tensors torch computes it as amax * fp32(1/448) (the divisor becomes a
+    reciprocal multiply); on CPU tensors as an IEEE division. The reference
+    runs on CUDA, so "cuda" is the default; "ieee" reproduces a CPU run."""
     x = x.astype(f32)
     amax = f32(np.abs(x).max()) if x.size else f32(0.0)
-    scale = f32(max(fdiv(amax, f32(448.0)), FLT_MIN))
+    if scalar_div == "cuda":
+        raw = f32(amax * (f32(1.0) / f32(448.0)))
+    else:
+        raw = fdiv(amax, f32(448.0))
+    scale = f32(max(raw, FLT_MIN))
     codes = e4m3_from_f32(np.clip(fdiv(x, scale), -E4M3_MAX, E4M3_MAX))
     return codes, scale
 

@@ -305,9 +305,21 @@ def gen_quant(ref: Path):
             actual, actual_scale = quant.quantize_activation(sample)
             assert torch.equal(actual_scale, scale)
             assert torch.equal(actual.view(torch.uint8), expected.view(torch.uint8))
+            # On CUDA, torch evaluates `amax / 448.0` as amax * fp32(1/448)
+            # (BinaryDivTrueKernel.cu: a CPU-scalar divisor becomes a
+            # reciprocal multiply); on these CPU tensors it divided. Record
+            # the CUDA-semantics result too, packed by the reference's own
+            # _pack kernel with that scale.
+            amax = peak.activation_abs_peak(sample)
+            cuda_scale = (amax * (torch.tensor(1.0) / 448.0)).clamp_min(
+                torch.finfo(torch.float32).tiny)
+            cuda_q = torch.empty_like(sample, dtype=torch.float8_e4m3fn)
+            quant._pack[((sample.numel() + 4095) // 4096,)](sample, cuda_q, cuda_scale,
+                                                            sample.numel(), 4096)
             out.update({f"c{idx}_x": bits(sample), f"c{idx}_dtype": np.array(
                 0 if dtype == torch.bfloat16 else 1), f"c{idx}_q": bits(actual),
-                f"c{idx}_scale": actual_scale.reshape(1).numpy()})
+                f"c{idx}_scale": actual_scale.reshape(1).numpy(),
+                f"c{idx}_q_cuda": bits(cuda_q), f"c{idx}_scale_cuda": cuda_scale.reshape(1).numpy()})
             idx += 1
     out["ncases"] = np.array(idx)
     np.savez_compressed(OUT / "fp8_quant.npz", **out)

@@ -119,9 +119,12 @@ def test_fp8_quant_golden():
     for i in range(int(g["ncases"])):
         raw = g[f"c{i}_x"]
         x = bf(raw) if int(g[f"c{i}_dtype"]) == 0 else raw.view(np.float16).astype(np.float32)
-        codes, scale = of.quantize_per_tensor(x)
+        codes, scale = of.quantize_per_tensor(x, scalar_div="ieee")  # the CPU run
         assert np.float32(scale) == g[f"c{i}_scale"][0], i
         assert np.array_equal(codes, g[f"c{i}_q"]), i
+        codes, scale = of.quantize_per_tensor(x, scalar_div="cuda")  # CUDA semantics
+        assert np.float32(scale) == g[f"c{i}_scale_cuda"][0], i
+        assert np.array_equal(codes, g[f"c{i}_q_cuda"]), i
 
 
 def test_e4m3_decode_table_finite():

@@ -135,12 +135,16 @@ class H3AttentionBackendB200:
     """Model-local attention backend: `precision="sage"` (INT8 QK / FP8 PV,
     the H3SageCUDA slot) or `"bf16"` (the H3DenseCUDA slot)."""
 
+    # run_phaa_attention may pass `out=` (a bf16 view of its send buffer)
+    writes_into = True
+
     def __init__(self, precision: str = "sage"):
         if precision not in ("sage", "bf16"):
             raise ValueError(f"Unsupported H3 attention precision: {precision}")
         self.precision = precision
         self.calls = 0
         self.kernel_calls = 0
+        self._ws = None
 
     def _kernel_eligible(self, query, key, value, attn_mask) -> bool:
         return (attn_mask is None and query.is_cuda and query.shape[-1] == HEAD_DIM
@@ -150,15 +154,25 @@ class H3AttentionBackendB200:
                 and all(t.stride(-1) == 1 for t in (query, key, value))
                 and (self.precision == "bf16" or query.shape == key.shape))
 
-    def __call__(self, query, key, value, *, attn_mask=None, head_offset=0):
-        if self._kernel_eligible(query, key, value, attn_mask):
+    def __call__(self, query, key, value, *, attn_mask=None, head_offset=0, out=None):
+        if self._kernel_eligible(query, key, value, attn_mask) and (
+                out is None or query.dtype == torch.bfloat16):
             if self.precision == "sage":
-                output = sage_attention(query, key, value)
+                b, h, s, _ = query.shape
+                key_ = (b, h, s, query.device)
+                if self._ws is None:
+                    self._ws = {}
+                if key_ not in self._ws:
+                    self._ws[key_] = SageWorkspace(b, h, s, query.device)
+                output = sage_attention(query, key, value, out=out, ws=self._ws[key_])
             else:
-                output = dense_attention(query, key, value)
+                output = dense_attention(query, key, value, out=out)
             self.kernel_calls += 1
             output = output.to(query.dtype) if output.dtype != query.dtype else output
         else:
             output = F.scaled_dot_product_attention(query, key, value, attn_mask=attn_mask)
+            if out is not None:
+                out.copy_(output)
+                output = out
         self.calls += 1
         return output

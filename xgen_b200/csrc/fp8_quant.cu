@@ -3,7 +3,7 @@
 // Per-tensor (the reference's scheme, x_base/x_base/operator/h3_fp8.py:9-12,
 // h3_fp8_quant.py:9-25, h3_abs_peak.py:14-25):
 //   peaks[b] = max |x| over block b            (NaN-propagating)
-//   scale    = max(max(peaks) / 448, FLT_MIN)
+//   scale    = max(max(peaks) * fp32(1/448), FLT_MIN)   (torch CUDA scalar division)
 //   out      = e4m3(clamp(x / scale, +-448))   (IEEE division, RNE)
 // The max is order-independent, so the result is bit-exact with the
 // reference whatever the block split; the per-block peaks live in a
@@ -73,7 +73,10 @@ __global__ void __launch_bounds__(kThreads) peak_to_scale_kernel(const int* __re
   if (threadIdx.x == 0) {
     int r = 0;
     for (int w = 0; w < kThreads / 32; ++w) r = max(r, warp_peak[w]);
-    const float s = __fdiv_rn(__int_as_float(r), 448.0f);
+    // torch evaluates `amax / 448.0` on a CUDA tensor as amax * fp32(1/448)
+    // (a CPU-scalar divisor is turned into a reciprocal multiply), which is
+    // what the reference's GPU path and its bit-equality test see.
+    const float s = __fmul_rn(__int_as_float(r), 1.0f / 448.0f);
     *scale = isnan(s) ? s : fmaxf(s, FLT_MIN);  // clamp_min keeps NaN
   }
 }

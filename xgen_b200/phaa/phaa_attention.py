@@ -1,0 +1,179 @@
+"""PHAA: head-chunked Ulysses attention with the A2A overlapped on a side stream.
+
+Mirror of `run_phaa_attention` (x_base/x_base/phaa/phaa_attention.py:38-366)
+for the options the H3 CUDA recipes use: bf16 or FP8 wire exchange, natural
+or tail-first chunk order, gather priority, a separate scatter stream/group,
+device or host join. The local heads are split into `phaa_split_num` chunks
+(remainder to the first chunks); chunk i+1's gather A2A runs on
+`comm_stream` while chunk i's attention runs on the compute stream, and each
+chunk's output returns by its own A2A.
+
+B200 extension: `fuse_rope=True` with `rotary_emb=(cos, sin)` applies the
+partial RoPE to Q and K inside the FP8 wire encode (the reference applies it
+in a separate pass before PHAA; the bytes on the wire are identical).
+"""
+from __future__ import annotations
+
+from contextlib import nullcontext
+
+import torch
+import torch.distributed as dist
+
+from ..sp.padding import get_pad_manager
+from . import fp8_transport as fp8
+
+
+class _HostStreams:
+    """Stream/event stand-ins for CPU tensors (gloo tests): ops are synchronous."""
+
+    class Event:
+        def record(self, *a):
+            pass
+
+    @staticmethod
+    def current_stream():
+        return _HostStreams._Stream()
+
+    class _Stream:
+        def wait_stream(self, *a):
+            pass
+
+        def wait_event(self, *a):
+            pass
+
+        def synchronize(self):
+            pass
+
+        def record_event(self):
+            return _HostStreams.Event()
+
+    @staticmethod
+    def stream(s):
+        return nullcontext()
+
+
+def chunk_sizes(heads_per_device: int, split: int) -> list[int]:
+    base, rem = divmod(heads_per_device, split)
+    return [base + (1 if i < rem else 0) for i in range(split)]
+
+
+def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, heads,
+                       phaa_split_num, head_dim, rope_fn=None, rotary_emb=None,
+                       attention_mask=None, pad_key="pad", attention_fn=None,
+                       fp8_transport=False, gather_priority=False, scatter_stream=None,
+                       scatter_group=None, tail_first=False, device_join=False,
+                       fuse_rope=False):
+    """query/key/value (B, S_loc, heads*head_dim) -> (B, S_loc, heads*head_dim)."""
+    W_S = sp_size
+    B, Sq, H = query.shape
+    D = head_dim
+    if attention_fn is None:
+        raise ValueError("PHAA on B200 requires a model-local attention_fn")
+    if fuse_rope and (not fp8_transport or rotary_emb is None):
+        raise ValueError("fused PHAA RoPE requires FP8 transport and rotary_emb")
+    if gather_priority and not fp8_transport:
+        raise ValueError("PHAA gather priority requires FP8 transport")
+    if device_join and (not fp8_transport or scatter_stream is not None):
+        raise ValueError("PHAA device join requires single-stream FP8 transport")
+    if (scatter_stream is None) != (scatter_group is None) or (
+            scatter_stream is not None and not fp8_transport):
+        raise ValueError("Separate PHAA scatter requires FP8, a stream and a process group")
+    if fp8_transport and query.device.type != "cuda":
+        raise ValueError("PHAA FP8 transport requires CUDA")
+
+    hpd = heads // W_S
+    sizes = chunk_sizes(hpd, phaa_split_num)
+    offsets = [sum(sizes[:i]) for i in range(phaa_split_num)]
+    order = list(range(phaa_split_num))
+    if tail_first:
+        if not fp8_transport or phaa_split_num != 4:
+            raise ValueError("PHAA tail-first requires FP8 transport and four chunks")
+        order = [3, 0, 1, 2]
+    pad = get_pad_manager().get_or_default(pad_key, 0)
+    acc = torch.cuda if query.device.type == "cuda" else _HostStreams
+    output_stream = scatter_stream if scatter_stream is not None else comm_stream
+    output_group = scatter_group if scatter_group is not None else sp_group
+
+    def exchange_one(out, inp, group):
+        if fp8_transport:
+            fp8.fp8_all_to_all(out, inp, D, group)
+        else:
+            dist.all_to_all_single(out, inp.contiguous(), group=group)
+
+    q5 = query.unflatten(-1, (heads, D)).unflatten(2, (W_S, hpd))
+    k5 = key.unflatten(-1, (heads, D)).unflatten(2, (W_S, hpd))
+    v5 = value.unflatten(-1, (heads, D)).unflatten(2, (W_S, hpd))
+    chunks = []
+    for c in range(phaa_split_num):
+        o, cs = offsets[c], sizes[c]
+        chunks.append(tuple(t[:, :, :, o:o + cs, :].permute(2, 1, 0, 3, 4) for t in (q5, k5, v5)))
+    gather = [tuple(torch.empty((W_S, Sq, B, cs, D), device=query.device, dtype=query.dtype)
+                    for _ in range(3)) for cs in sizes]
+    returned = [torch.empty((W_S, Sq, B, cs * D), device=query.device, dtype=query.dtype)
+                for cs in sizes]
+    gathered = [acc.Event() for _ in sizes]
+    attended = [acc.Event() for _ in sizes]
+    results = [None] * phaa_split_num
+
+    def gather_chunk(i):
+        if fp8_transport:
+            fp8.fp8_all_to_all_many(gather[i], chunks[i], D, sp_group,
+                                    rotary_emb=rotary_emb if fuse_rope else None)
+        else:
+            for out, inp in zip(gather[i], chunks[i]):
+                exchange_one(out, inp, sp_group)
+        gathered[i].record(comm_stream)
+
+    comm_stream.wait_stream(acc.current_stream())
+    if scatter_stream is not None:
+        scatter_stream.wait_stream(acc.current_stream())
+    with acc.stream(comm_stream):
+        for i in (order if gather_priority else order[:1]):
+            gather_chunk(i)
+
+    for pos, step in enumerate(order):
+        acc.current_stream().wait_event(gathered[step])
+        qv, kv, vv = (x.flatten(0, 1).permute(1, 2, 0, 3) for x in gather[step])
+        if pad > 0:
+            qv, kv, vv = (x.narrow(2, 0, x.shape[2] - pad) for x in (qv, kv, vv))
+        if rope_fn is not None and rotary_emb is not None and not fuse_rope:
+            qv, kv = rope_fn(qv, kv, *rotary_emb)
+        cs = sizes[step]
+        if getattr(attention_fn, "writes_into", False):
+            # The kernel epilogue stores straight into the return-A2A send
+            # layout (W_S, S, B, cs, D): no reshape/pad copies.
+            send = torch.empty((W_S, Sq, B, cs, D), device=query.device, dtype=query.dtype)
+            if pad > 0:
+                send[-1, Sq - pad:].zero_()
+            view = send.flatten(0, 1).permute(1, 2, 0, 3)
+            attention_fn(qv, kv, vv, head_offset=offsets[step], attn_mask=attention_mask,
+                         out=view.narrow(2, 0, W_S * Sq - pad))
+            results[step] = send.flatten(-2, -1)
+        else:
+            out = attention_fn(qv, kv, vv, head_offset=offsets[step], attn_mask=attention_mask)
+            out = out.type_as(query)
+            if pad > 0:
+                shape = list(out.shape)
+                shape[2] = pad
+                out = torch.cat([out, out.new_zeros(shape)], dim=2)
+            results[step] = out.unflatten(2, (W_S, -1)).permute(2, 3, 0, 1, 4).flatten(-2, -1)
+        attended[step].record()
+        with acc.stream(comm_stream):
+            if not gather_priority and pos + 1 < phaa_split_num:
+                gather_chunk(order[pos + 1])
+            ctx = acc.stream(scatter_stream) if scatter_stream is not None else nullcontext()
+            with ctx:
+                output_stream.wait_event(attended[step])
+                exchange_one(returned[step], results[step], output_group)
+                if device_join:
+                    results[step].record_stream(comm_stream)
+                    for t in chunks[step]:
+                        t.record_stream(comm_stream)
+
+    if device_join:
+        acc.current_stream().wait_stream(comm_stream)
+    else:
+        comm_stream.synchronize()
+    if scatter_stream is not None:
+        scatter_stream.synchronize()
+    return torch.cat([b.permute(2, 1, 0, 3) for b in returned], dim=3).flatten(-2, -1)
