@@ -54,7 +54,46 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only the attention kernel on --seq/--heads (profiling case)")
+    ap.add_argument("--seq", type=int, default=SEQ)
+    ap.add_argument("--heads", type=int, default=HEADS)
     return ap.parse_args()
+
+
+def kernel_only(args):
+    """Prepare once, then run the attention kernel W + K times on a
+    [1, heads, seq, 128] problem; prints its mean time (the ncu case)."""
+    import torch
+
+    from xgen_b200.attention import dense_attention, kernel_errors, sage_attention_prepared, sage_prepare
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    shape = (1, args.heads, args.seq, HEAD_DIM)
+    q = torch.randn(shape, device=dev, generator=g).bfloat16()
+    k = (torch.randn(shape, device=dev, generator=g) + 2 * torch.randn(1, args.heads, 1, HEAD_DIM, device=dev, generator=g)).bfloat16()
+    v = torch.randn(shape, device=dev, generator=g).bfloat16()
+    out = torch.empty_like(q)
+    if args.precision == "sage":
+        ws = sage_prepare(q, k, v)
+        run = lambda: sage_attention_prepared(ws, out)  # noqa: E731
+    else:
+        run = lambda: dense_attention(q, k, v, out=out)  # noqa: E731
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    flops = 4.0 * args.seq * args.seq * HEAD_DIM * args.heads
+    assert kernel_errors(dev) == 0
+    print(json.dumps({"kernel": f"attention_{args.precision}", "seq": args.seq, "heads": args.heads,
+                      "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
 
 
 # ------------------------------------------------------------------ helpers
@@ -185,6 +224,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel_only:
+        return kernel_only(args)
 
     import torch
     import torch.distributed as dist
