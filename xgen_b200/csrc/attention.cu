@@ -28,6 +28,8 @@
 // issue order: S_i(j+1) is issued after PV_i(j), which reads P_i(j) from the
 // same TMEM columns. The commit that publishes S_i(j+1) therefore also
 // certifies PV_i(j) complete, so the softmax warps may rescale O_i then.
+#include <climits>
+
 #include "sm100.cuh"
 #include "tma_host.h"
 
@@ -44,6 +46,8 @@ constexpr int kThreads = 320;
 constexpr int kTmaWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr float kNegInf = -__builtin_huge_valf();
+// log2(448 / 2^4): e4m3 P = exp2(x + kLog2PScale) spans up to 448 under kTau = 4.
+constexpr float kLog2PScale = 4.807354922057604f;
 
 template <bool kSage>
 struct Cfg {
@@ -276,25 +280,52 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, r[c]);
       tmem_ld_wait();
+      // Row max of this tile, on the raw accumulators: the score scale is
+      // positive, so max(scale * s) = scale * max(s) (integer max for Sage).
+      const int valid = p.seq_kv - j * kBN;  // keys >= valid are padding
+      const bool tail = valid < kBN;
       float comb0 = p.scale_log2, comb1 = p.scale_log2;
+      float mt;
       if constexpr (kSage) {
         comb0 = qs * p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + 2 * j];
         comb1 = qs * p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + 2 * j + 1];
-      }
-      const int valid = p.seq_kv - j * kBN;  // keys >= valid are padding
-      float mt = kNegInf;
+        int mx0 = INT_MIN, mx1 = INT_MIN;
+        if (!tail) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+          for (int e = 0; e < 32; ++e) {
+            mx0 = max(mx0, max(static_cast<int>(r[0][e]), static_cast<int>(r[1][e])));
+            mx1 = max(mx1, max(static_cast<int>(r[2][e]), static_cast<int>(r[3][e])));
+          }
+        } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int col = c * 32 + e;
-          float v;
-          if constexpr (kSage) v = static_cast<float>(static_cast<int>(r[c][e])) * (col < 64 ? comb0 : comb1);
-          else v = __uint_as_float(r[c][e]) * comb0;
-          if (col >= valid) v = kNegInf;
-          r[c][e] = __float_as_uint(v);
-          mt = fmaxf(mt, v);
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int col = c * 32 + e;
+              if (col < valid) {
+                if (c < 2) mx0 = max(mx0, static_cast<int>(r[c][e]));
+                else mx1 = max(mx1, static_cast<int>(r[c][e]));
+              }
+            }
         }
+        mt = fmaxf(mx0 == INT_MIN ? kNegInf : comb0 * static_cast<float>(mx0),
+                   mx1 == INT_MIN ? kNegInf : comb1 * static_cast<float>(mx1));
+      } else {
+        float m0 = kNegInf, m1 = kNegInf;
+        if (!tail) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            m0 = fmaxf(m0, fmaxf(__uint_as_float(r[0][e]), __uint_as_float(r[1][e])));
+            m1 = fmaxf(m1, fmaxf(__uint_as_float(r[2][e]), __uint_as_float(r[3][e])));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e < valid) m0 = fmaxf(m0, __uint_as_float(r[c][e]));
+        }
+        mt = fmaxf(m0, m1) * comb0;
       }
       // Lazy rescale decision (warp-uniform TMEM traffic).
       const float m_new = fmaxf(m_used, mt);
@@ -316,35 +347,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      // P = exp2(s - m_used), row sum, pack and store over S.
+      // P = exp2(scale*s - m_used) (times kPScale for e4m3, folded into the
+      // exponent), row sum, pack and store over S.
       float rs = 0.f;
       uint32_t packed[32];
       if constexpr (kSage) {
+        // exp2 on packed halves: the f16 argument keeps ~1e-3 relative
+        // accuracy for |x| < 16, finer than the e4m3 P it feeds.
+        const float off = kLog2PScale - m_used;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
+          const float comb = c < 2 ? comb0 : comb1;
+          // f16x2 partial sums over 8 pairs each (<= 8 * 448), then fp32.
+          __half2 hsum0 = __float2half2_rn(0.f), hsum1 = hsum0;
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
-            float pv[4];
+            float x[4];
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-              pv[t] = ex2_approx(__uint_as_float(r[c][e + t]) - m_used);
-              rs += pv[t];
+              x[t] = fmaf(static_cast<float>(static_cast<int>(r[c][e + t])), comb, off);
+              if (tail && c * 32 + e + t >= valid) x[t] = kNegInf;
             }
-            const uint32_t lo = pack_e4m3x2(pv[0] * C::kPScale, pv[1] * C::kPScale);
-            const uint32_t hi = pack_e4m3x2(pv[2] * C::kPScale, pv[3] * C::kPScale);
-            packed[c * 8 + e / 4] = lo | (hi << 16);
+            const uint32_t e01 = ex2_f16x2(pack_f16x2(x[0], x[1]));
+            const uint32_t e23 = ex2_f16x2(pack_f16x2(x[2], x[3]));
+            hsum0 = __hadd2(hsum0, *reinterpret_cast<const __half2*>(&e01));
+            hsum1 = __hadd2(hsum1, *reinterpret_cast<const __half2*>(&e23));
+            packed[c * 8 + e / 4] = e4m3x2_from_f16x2(e01) | (e4m3x2_from_f16x2(e23) << 16);
           }
+          const float2 f0 = __half22float2(hsum0), f1 = __half22float2(hsum1);
+          rs += (f0.x + f0.y) + (f1.x + f1.y);
         }
         tmem_st32(s_addr, packed);
       } else {
+        const float off = -m_used;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              const float a = ex2_approx(__uint_as_float(r[half * 2 + c][e]) - m_used);
-              const float b = ex2_approx(__uint_as_float(r[half * 2 + c][e + 1]) - m_used);
+              const int col = (half * 2 + c) * 32 + e;
+              float xa = fmaf(__uint_as_float(r[half * 2 + c][e]), comb0, off);
+              float xb = fmaf(__uint_as_float(r[half * 2 + c][e + 1]), comb0, off);
+              if (tail) {
+                if (col >= valid) xa = kNegInf;
+                if (col + 1 >= valid) xb = kNegInf;
+              }
+              const float a = ex2_approx(xa);
+              const float b = ex2_approx(xb);
               rs += a + b;
               packed[c * 16 + e / 2] = pack_bf16x2(a, b);
             }
@@ -375,9 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; e += 2) {
             float x0 = __uint_as_float(o[e]) * inv_l;
             float x1 = __uint_as_float(o[e + 1]) * inv_l;
-            if constexpr (kSage) {
-              x0 *= p.v_scale[static_cast<int64_t>(bh) * kD + c * 32 + e] * (1.0f / C::kPScale);
-              x1 *= p.v_scale[static_cast<int64_t>(bh) * kD + c * 32 + e + 1] * (1.0f / C::kPScale);
+            if constexpr (kSage) {  // l sums the same kPScale-scaled P
+              x0 *= p.v_scale[static_cast<int64_t>(bh) * kD + c * 32 + e];
+              x1 *= p.v_scale[static_cast<int64_t>(bh) * kD + c * 32 + e + 1];
             }
             w[e / 2] = pack_bf16x2(x0, x1);
           }

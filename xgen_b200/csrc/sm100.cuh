@@ -282,6 +282,27 @@ __device__ __forceinline__ uint32_t pack_e4m3x2(float lo, float hi) {
   return r;
 }
 
+// Two fp32 -> packed f16x2 (lo in bits 0-15), RNE.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// exp2 of both halves of an f16x2 (one MUFU op for two values).
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// f16x2 -> e4m3x2 (low half -> low byte), RNE, saturating.
+__device__ __forceinline__ uint32_t e4m3x2_from_f16x2(uint32_t x) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(x));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
