@@ -5,14 +5,19 @@
 // SDPA for the BF16 recipe (x_base/x_base/operator/attention.py:357-375,
 // h3_sage_cuda.py:21-25, h3_dense_cuda.py:11-15).
 //
-// CTA = two 128-row Q tiles of one (batch, head); KV tiles of 128 keys.
+// CTA = two 128-row Q tiles of one (batch, head); KV tiles of 64 keys.
 //   warps 0-3  softmax for Q tile 0 (TMEM lanes 0-127)
 //   warps 4-7  softmax for Q tile 1
 //   warp  8    TMA producer (Q once, then a K/V ring of kStages stages)
-//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
-// TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each. P_i is
-// written over the first columns of S_i and read by the P.V MMA straight from
-// TMEM (A operand in TMEM), so P never touches shared memory.
+//   warp  9    TMEM allocator + tcgen05.mma issuer for Q tile 0
+//   warp 10    tcgen05.mma issuer for Q tile 1 (independent streams, so one
+//              tile's S(t+2) never waits on the other tile's softmax)
+// TMEM (512 columns): S0a | S0b | S1a | S1b (64 fp32 columns each) | O0 | O1
+// (128 each). Each Q tile double-buffers S: while its softmax works on KV
+// tile t (buffer t%2) the tensor core already holds S(t+1) in the other
+// buffer and computes S(t+2) once PV(t) has consumed P(t). P(t) is written
+// over the first columns of its S buffer and read by the P.V MMA straight
+// from TMEM (A operand in TMEM), so P never touches shared memory.
 //
 // Sage variant: S = int8 Q . int8 K^T (kind::i8, s32 accumulate), scores
 // dequantised per 64-row Q block x 64-key K block (sm_scale*log2e folded into
@@ -22,12 +27,14 @@
 //
 // Online softmax in the exp2 domain with lazy rescaling: a row's running max
 // only moves (and O is rescaled in TMEM) when a tile raises it by more than
-// kTau (log2 units), so P <= 2^kTau.
+// kTau (log2 units), so P <= 2^kTau. A rescale first waits for the previous
+// tile's P.V (pv_done) so O is stable: when S(t) is visible, PV(t-2) has
+// completed, so pv_done is at most one phase behind and its parity wait is
+// exact.
 //
 // Ordering relies on tcgen05.mma ops issued by one thread executing in
-// issue order: S_i(j+1) is issued after PV_i(j), which reads P_i(j) from the
-// same TMEM columns. The commit that publishes S_i(j+1) therefore also
-// certifies PV_i(j) complete, so the softmax warps may rescale O_i then.
+// issue order: S_i(t+2) is issued by tile i's issuer after PV_i(t), which
+// reads P_i(t) from the same TMEM columns.
 #include <climits>
 
 #include "sm100.cuh"
@@ -38,31 +45,43 @@ namespace attn {
 
 using namespace sm100;
 
-constexpr int kBM = 128;
-constexpr int kQT = 2;
-constexpr int kBN = 128;
+constexpr int kBM = 128;  // rows per Q tile
+constexpr int kQT = 2;    // Q tiles per CTA
+constexpr int kBN = 64;   // keys per KV tile
 constexpr int kD = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kTmaWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kMmaWarp = 9;  // warps 9 and 10 issue the MMAs of Q tiles 0 and 1
 constexpr float kNegInf = -__builtin_huge_valf();
 // log2(448 / 2^4): e4m3 P = exp2(x + kLog2PScale) spans up to 448 under kTau = 4.
 constexpr float kLog2PScale = 4.807354922057604f;
+// With kPolyEvery > 0, one exp2 in kPolyEvery goes to the FMA pipe
+// (ex2_poly) instead of MUFU. Measured on B200 at this tile shape it only
+// adds issue pressure (MUFU is not the limiter once the exp sections
+// ping-pong), so it is off by default.
+#ifndef XGB_ATTN_POLY_EVERY
+#define XGB_ATTN_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = XGB_ATTN_POLY_EVERY;
+__device__ __forceinline__ bool use_poly(int idx) {
+  return kPolyEvery > 0 && idx % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1;
+}
 
 template <bool kSage>
 struct Cfg {
   static constexpr int kElem = kSage ? 1 : 2;
-  static constexpr int kTileBytes = kBM * kD * kElem;  // one 128x128 tile
-  static constexpr int kSubTiles = kSage ? 1 : 2;      // 128-byte wide TMA boxes per tile
-  static constexpr int kStages = kSage ? 4 : 2;
-  static constexpr int kKSteps = kSage ? 4 : 8;        // MMA K steps over D (and over keys)
+  static constexpr int kQBytes = kBM * kD * kElem;   // one 128-row Q tile
+  static constexpr int kKVBytes = kBN * kD * kElem;  // one 64-key K or V tile
+  static constexpr int kSub = kBN * 128;             // bytes of one 128-byte-wide TMA box of K/V
+  static constexpr int kStages = kSage ? 8 : 4;
+  static constexpr int kKStepsD = kSage ? 4 : 8;     // QK^T MMA steps over D (32 B each)
+  static constexpr int kKStepsN = kSage ? 2 : 4;     // P.V MMA steps over the 64 keys
   static constexpr float kTau = kSage ? 4.0f : 8.0f;
-  static constexpr float kPScale = kSage ? 448.0f / 16.0f : 1.0f;  // 448 / 2^kTau for e4m3
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQT * kTileBytes;
-  static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
-  static constexpr int kSmem = kBarOff + 256 + 1024;  // + barriers + alignment slack
+  static constexpr int kKOff = kQOff + kQT * kQBytes;
+  static constexpr int kVOff = kKOff + kStages * kKVBytes;
+  static constexpr int kBarOff = kVOff + kStages * kKVBytes;
+  static constexpr int kSmem = kBarOff + 512 + 1024;  // + barriers + alignment slack
   static constexpr uint32_t kIdescQK =
       kSage ? instr_desc(2, 1, 1, false, false, kBM, kBN) : instr_desc(1, 1, 1, false, false, kBM, kBN);
   static constexpr uint32_t kIdescPV =
@@ -87,34 +106,39 @@ struct Params {
 
 struct Barriers {
   uint64_t q_full;
-  uint64_t k_full[4];
-  uint64_t v_full[4];
-  uint64_t kv_empty[4];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t o_full[2];
-  uint64_t end;
+  uint64_t k_full[8];
+  uint64_t v_full[8];
+  uint64_t kv_empty[8];
+  uint64_t s_full[2][2];  // [Q tile][S buffer]
+  uint64_t p_full[2][2];
+  uint64_t pv_done[2];
+  uint64_t o_done[2];  // every P.V of Q tile i has landed in O_i
+  uint64_t turn[2];    // exp-section ping-pong between the softmax warpgroups
+  uint64_t end[2];
   uint32_t tmem_base;
 };
 
+// TMEM column of S/P buffer `b` of Q tile `i`, and of O_i.
+__device__ __forceinline__ uint32_t s_col(int i, int b) { return static_cast<uint32_t>(i * 128 + b * 64); }
+__device__ __forceinline__ uint32_t o_col(int i) { return static_cast<uint32_t>(256 + i * 128); }
+
 template <bool kSage>
-__device__ __forceinline__ void load_tile(const CUtensorMap* map, uint8_t* dst, uint64_t* bar,
-                                          int row, int bh, int heads) {
+__device__ __forceinline__ void load_rows(const CUtensorMap* map, uint8_t* dst, uint64_t* bar,
+                                          int row, int bh, int heads, int sub_bytes) {
   if constexpr (kSage) {
     tma_load_3d(dst, map, bar, 0, row, bh);
   } else {
     const int b = bh / heads, h = bh % heads;
     tma_load_4d(dst, map, bar, 0, row, h, b);
-    tma_load_4d(dst + 16384, map, bar, 64, row, h, b);
+    tma_load_4d(dst + sub_bytes, map, bar, 64, row, h, b);
   }
 }
 
-// K-major SW128 descriptor of MMA K-step `k` within a 128x128 tile.
+// K-major SW128 descriptor of MMA K-step `k` (32 bytes of D) within a tile
+// whose 128-byte-wide sub-tiles (bf16: d 0-63, d 64-127) are `sub_bytes` apart.
 template <bool kSage>
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_saddr, int k) {
-  // 32 bytes of K per step; bf16 tiles hold d 0-63 and d 64-127 in two
-  // 16 KB sub-tiles.
-  const uint32_t sub = kSage ? 0u : static_cast<uint32_t>(k >> 2) * 16384u;
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_saddr, int k, uint32_t sub_bytes) {
+  const uint32_t sub = kSage ? 0u : static_cast<uint32_t>(k >> 2) * sub_bytes;
   const uint32_t off = static_cast<uint32_t>(kSage ? k : (k & 3)) * 32u;
   return smem_desc_sw128(tile_saddr + sub + off, 16, 1024);
 }
@@ -122,9 +146,10 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_saddr, int k) {
 // MN-major SW128 descriptor of the V tile for MMA K-step `k` (keys).
 template <bool kSage>
 __device__ __forceinline__ uint64_t vdesc(uint32_t tile_saddr, int k) {
-  // keys per step: 32 (e4m3) or 16 (bf16); each key row is 128 B per sub-tile.
+  // keys per step: 32 (e4m3) or 16 (bf16); each key row is 128 B per sub-tile;
+  // the bf16 d 64-127 sub-tile sits kSub bytes after d 0-63.
   const uint32_t off = static_cast<uint32_t>(k) * (kSage ? 32u : 16u) * 128u;
-  return smem_desc_sw128(tile_saddr + off, 16384, 1024);
+  return smem_desc_sw128(tile_saddr + off, Cfg<kSage>::kSub, 1024);
 }
 
 template <bool kSage>
@@ -148,14 +173,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->kv_empty[s], 2);  // released by both issuers
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], kBM);
-      mbar_init(&bars->o_full[i], 1);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&bars->s_full[i][b], 1);
+        mbar_init(&bars->p_full[i][b], kBM);
+      }
+      mbar_init(&bars->pv_done[i], 1);
     }
-    mbar_init(&bars->end, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->o_done[i], 1);
+      mbar_init(&bars->end[i], 1);
+      mbar_init(&bars->turn[i], kBM);
+    }
     fence_barrier_init();
   }
   if (warp == kMmaWarp) tmem_alloc<512>(&bars->tmem_base);
@@ -173,166 +204,157 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(&bars->q_full, kQT * C::kTileBytes);
+      mbar_arrive_expect_tx(&bars->q_full, kQT * C::kQBytes);
       for (int i = 0; i < kQT; ++i)
-        load_tile<kSage>(&q_map, smem + C::kQOff + i * C::kTileBytes, &bars->q_full, m0 + i * kBM,
-                         bh, p.heads);
+        load_rows<kSage>(&q_map, smem + C::kQOff + i * C::kQBytes, &bars->q_full, m0 + i * kBM,
+                         bh, p.heads, kBM * 128);
       int issued = 0;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j % C::kStages;
-        if (j >= C::kStages) ok = mbar_wait(&bars->kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
+      for (int t = 0; t < n_kv && ok; ++t) {
+        const int s = t % C::kStages;
+        if (t >= C::kStages) ok = mbar_wait(&bars->kv_empty[s], ((t / C::kStages) - 1) & 1, p.err);
         if (!ok) break;
-        mbar_arrive_expect_tx(&bars->k_full[s], C::kTileBytes);
-        load_tile<kSage>(&k_map, smem + C::kKOff + s * C::kTileBytes, &bars->k_full[s], j * kBN, bh,
-                         p.heads);
-        mbar_arrive_expect_tx(&bars->v_full[s], C::kTileBytes);
-        load_tile<kSage>(&v_map, smem + C::kVOff + s * C::kTileBytes, &bars->v_full[s], j * kBN, bh,
-                         p.heads);
-        issued = j + 1;
+        mbar_arrive_expect_tx(&bars->k_full[s], C::kKVBytes);
+        load_rows<kSage>(&k_map, smem + C::kKOff + s * C::kKVBytes, &bars->k_full[s], t * kBN, bh,
+                         p.heads, C::kSub);
+        mbar_arrive_expect_tx(&bars->v_full[s], C::kKVBytes);
+        load_rows<kSage>(&v_map, smem + C::kVOff + s * C::kKVBytes, &bars->v_full[s], t * kBN, bh,
+                         p.heads, C::kSub);
+        issued = t + 1;
       }
       // Never leave with copies in flight: wait (bounded) for the last ones.
-      for (int j = max(0, issued - C::kStages); j < issued; ++j) {
-        const int s = j % C::kStages;
-        mbar_wait(&bars->k_full[s], (j / C::kStages) & 1, p.err, 100000000ull);
-        mbar_wait(&bars->v_full[s], (j / C::kStages) & 1, p.err, 100000000ull);
+      for (int t = max(0, issued - C::kStages); t < issued; ++t) {
+        const int s = t % C::kStages;
+        mbar_wait(&bars->k_full[s], (t / C::kStages) & 1, p.err, 100000000ull);
+        mbar_wait(&bars->v_full[s], (t / C::kStages) & 1, p.err, 100000000ull);
       }
       mbar_wait(&bars->q_full, 0, p.err, 100000000ull);
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+    // ------------------------------------------------------------ MMA issuers
+    const int i = warp - kMmaWarp;  // Q tile served by this issuer
     if (lane == 0) {
-      const uint32_t q_saddr = smem_u32(smem + C::kQOff);
+      const uint32_t qa = smem_u32(smem + C::kQOff) + i * C::kQBytes;
       const uint32_t k_saddr = smem_u32(smem + C::kKOff);
       const uint32_t v_saddr = smem_u32(smem + C::kVOff);
       constexpr Kind kQK = kSage ? Kind::kI8 : Kind::kF16;
       constexpr Kind kPV = kSage ? Kind::kF8F6F4 : Kind::kF16;
+      // S_i(t) -> buffer t%2 of Q tile i, publish on s_full[i][t%2].
+      auto issue_s = [&](int t) {
+        const uint32_t ka = k_saddr + (t % C::kStages) * C::kKVBytes;
+#pragma unroll
+        for (int k = 0; k < C::kKStepsD; ++k)
+          mma_ss<kQK>(tmem + s_col(i, t & 1), kmajor_desc<kSage>(qa, k, kBM * 128),
+                      kmajor_desc<kSage>(ka, k, C::kSub), C::kIdescQK, k > 0);
+        tc_commit(&bars->s_full[i][t & 1]);
+      };
       bool ok = mbar_wait(&bars->q_full, 0, p.err);
-      auto issue_s = [&](int i, int stage) {
-        const uint32_t qa = q_saddr + i * C::kTileBytes;
-        const uint32_t ka = k_saddr + stage * C::kTileBytes;
-#pragma unroll
-        for (int k = 0; k < C::kKSteps; ++k)
-          mma_ss<kQK>(tmem + i * 128, kmajor_desc<kSage>(qa, k), kmajor_desc<kSage>(ka, k),
-                      C::kIdescQK, k > 0);
-        tc_commit(&bars->s_full[i]);
-      };
-      auto issue_pv = [&](int i, int stage, bool acc) {
-        const uint32_t va = v_saddr + stage * C::kTileBytes;
-#pragma unroll
-        for (int k = 0; k < C::kKSteps; ++k)
-          mma_ts<kPV>(tmem + 256 + i * 128, tmem + i * 128 + k * 8, vdesc<kSage>(va, k),
-                      C::kIdescPV, acc || k > 0);
-      };
-      if (ok) {
-        ok = mbar_wait(&bars->k_full[0], 0, p.err);
-        if (ok) {
-          tc_fence_after();
-          issue_s(0, 0);
-          issue_s(1, 0);
-        }
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j % C::kStages;
-        const uint32_t ph = (j / C::kStages) & 1;
-        const int sn = (j + 1) % C::kStages;
-        const uint32_t phn = ((j + 1) / C::kStages) & 1;
-        ok = mbar_wait(&bars->v_full[s], ph, p.err) && mbar_wait(&bars->p_full[0], j & 1, p.err);
+      for (int t = 0; t < 2 && t < n_kv && ok; ++t) {
+        ok = mbar_wait(&bars->k_full[t % C::kStages], (t / C::kStages) & 1, p.err);
         if (!ok) break;
         tc_fence_after();
-        issue_pv(0, s, j > 0);
-        if (j + 1 < n_kv) {
-          ok = mbar_wait(&bars->k_full[sn], phn, p.err);
+        issue_s(t);
+      }
+      for (int t = 0; t < n_kv && ok; ++t) {
+        const int s = t % C::kStages;
+        ok = mbar_wait(&bars->v_full[s], (t / C::kStages) & 1, p.err) &&
+             mbar_wait(&bars->p_full[i][t & 1], (t >> 1) & 1, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        // O_i += P_i(t) . V(t)
+        const uint32_t va = v_saddr + s * C::kKVBytes;
+#pragma unroll
+        for (int k = 0; k < C::kKStepsN; ++k)
+          mma_ts<kPV>(tmem + o_col(i), tmem + s_col(i, t & 1) + k * 8, vdesc<kSage>(va, k),
+                      C::kIdescPV, t > 0 || k > 0);
+        tc_commit(&bars->pv_done[i]);
+        tc_commit(&bars->kv_empty[s]);
+        const int t2 = t + 2;
+        if (t2 < n_kv) {
+          ok = mbar_wait(&bars->k_full[t2 % C::kStages], (t2 / C::kStages) & 1, p.err);
           if (!ok) break;
           tc_fence_after();
-          issue_s(0, sn);
+          issue_s(t2);
         }
-        ok = mbar_wait(&bars->p_full[1], j & 1, p.err);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(1, s, j > 0);
-        tc_commit(&bars->kv_empty[s]);
-        if (j + 1 < n_kv) issue_s(1, sn);
       }
-      tc_commit(&bars->o_full[0]);
-      tc_commit(&bars->o_full[1]);
-      tc_commit(&bars->end);
-      mbar_wait(&bars->end, 0, p.err, 100000000ull);
+      tc_commit(&bars->o_done[i]);
+      tc_commit(&bars->end[i]);
+      mbar_wait(&bars->end[i], 0, p.err, 100000000ull);
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int i = warp >> 2;               // Q tile of this warpgroup
+    const int i = warp >> 2;                // Q tile of this warpgroup
     const int lane_base = (warp & 3) * 32;  // TMEM lane quarter of this warp
     const int row = m0 + i * kBM + lane_base + lane;
-    const uint32_t s_addr = tmem + (static_cast<uint32_t>(lane_base) << 16) + i * 128;
-    const uint32_t o_addr = tmem + (static_cast<uint32_t>(lane_base) << 16) + 256 + i * 128;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lane_base) << 16);
+    const uint32_t o_addr = lane_addr + o_col(i);
     float qs = 0.f;
     if constexpr (kSage) {
       if (row < p.scale_stride * 64) qs = p.q_scale[static_cast<int64_t>(bh) * p.scale_stride + row / 64];
     }
     float m_used = kNegInf;
     float l = 0.f;
+    float ks = 0.f;  // K-block scale of the current tile (Sage)
+    if constexpr (kSage) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride];
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[i], j & 1, p.err));
+    // The two warpgroups take turns in the MUFU-bound exp section so one's
+    // exp overlaps the other's load/max/rescale work; WG1 hands the first
+    // turn to WG0.
+    if (i == 1) mbar_arrive(&bars->turn[0]);
+    for (int t = 0; t < n_kv; ++t) {
+      const uint32_t s_addr = lane_addr + s_col(i, t & 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[i][t & 1], (t >> 1) & 1, p.err));
       if (!ok) break;
       tc_fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, r[c]);
+      uint32_t r[2][32];
+      tmem_ld32(s_addr, r[0]);
+      tmem_ld32(s_addr + 32, r[1]);
       tmem_ld_wait();
-      // Row max of this tile, on the raw accumulators: the score scale is
-      // positive, so max(scale * s) = scale * max(s) (integer max for Sage).
-      const int valid = p.seq_kv - j * kBN;  // keys >= valid are padding
-      const bool tail = valid < kBN;
-      float comb0 = p.scale_log2, comb1 = p.scale_log2;
-      float mt;
+      // Sage: int32 accumulators become exact floats 12582912 + s by adding
+      // 0x4B400000 to their bits (|s| < 2^22: 128 products of |int8| <=
+      // 127), a monotone map, so the max runs on floats and no conversion
+      // instruction is needed. Padding keys (>= valid, last tile only) get a
+      // sentinel far below any real score.
+      const int valid = p.seq_kv - t * kBN;
+      const float comb = kSage ? qs * ks : p.scale_log2;
       if constexpr (kSage) {
-        comb0 = qs * p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + 2 * j];
-        comb1 = qs * p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + 2 * j + 1];
-        int mx0 = INT_MIN, mx1 = INT_MIN;
-        if (!tail) {
+        if (t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + t + 1];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            mx0 = max(mx0, max(static_cast<int>(r[0][e]), static_cast<int>(r[1][e])));
-            mx1 = max(mx1, max(static_cast<int>(r[2][e]), static_cast<int>(r[3][e])));
-          }
-        } else {
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int col = c * 32 + e;
-              if (col < valid) {
-                if (c < 2) mx0 = max(mx0, static_cast<int>(r[c][e]));
-                else mx1 = max(mx1, static_cast<int>(r[c][e]));
-              }
-            }
-        }
-        mt = fmaxf(mx0 == INT_MIN ? kNegInf : comb0 * static_cast<float>(mx0),
-                   mx1 == INT_MIN ? kNegInf : comb1 * static_cast<float>(mx1));
-      } else {
-        float m0 = kNegInf, m1 = kNegInf;
-        if (!tail) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            m0 = fmaxf(m0, fmaxf(__uint_as_float(r[0][e]), __uint_as_float(r[1][e])));
-            m1 = fmaxf(m1, fmaxf(__uint_as_float(r[2][e]), __uint_as_float(r[3][e])));
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (c * 32 + e < valid) m0 = fmaxf(m0, __uint_as_float(r[c][e]));
-        }
-        mt = fmaxf(m0, m1) * comb0;
+          for (int e = 0; e < 32; ++e) r[c][e] += 0x4B400000u;
       }
-      // Lazy rescale decision (warp-uniform TMEM traffic).
+      if (valid < kBN) {
+        const uint32_t sentinel = kSage ? 0x4B000000u /* 12582912 - 2^22 */ : 0xFF800000u /* -inf */;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= valid) r[c][e] = sentinel;
+      }
+      // Four independent 3-input max chains, then combined.
+      float m4[4];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        m4[2 * c] = fmax3(__uint_as_float(r[c][0]), __uint_as_float(r[c][1]), __uint_as_float(r[c][2]));
+        m4[2 * c + 1] = fmax3(__uint_as_float(r[c][3]), __uint_as_float(r[c][4]), __uint_as_float(r[c][5]));
+#pragma unroll
+        for (int e = 6; e < 30; e += 4) {
+          m4[2 * c] = fmax3(m4[2 * c], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]));
+          m4[2 * c + 1] = fmax3(m4[2 * c + 1], __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]));
+        }
+        m4[2 * c] = fmax3(m4[2 * c], __uint_as_float(r[c][30]), __uint_as_float(r[c][31]));
+      }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      const float mt = kSage ? comb * (mx - 12582912.0f) : mx * comb;
+      // Lazy rescale (warp-uniform TMEM traffic); O must hold PV(t-1).
       const float m_new = fmaxf(m_used, mt);
       const bool need = m_new > m_used + C::kTau;
-      if (j == 0) {
+      if (t == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, need)) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i], (t - 1) & 1, p.err));
+        if (!ok) break;
+        tc_fence_after();
         const float alpha = need ? ex2_approx(m_used - m_new) : 1.0f;
         if (need) m_used = m_new;
         l *= alpha;
@@ -347,68 +369,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      // P = exp2(scale*s - m_used) (times kPScale for e4m3, folded into the
-      // exponent), row sum, pack and store over S.
-      float rs = 0.f;
-      uint32_t packed[32];
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->turn[i], t & 1, p.err));
+      if (!ok) break;
+      // P = exp2(comb*s - m_used) (times kPScale for e4m3, folded into the
+      // exponent), row sum, pack and store over the S buffer.
+      float rs0 = 0.f, rs1 = 0.f;
       if constexpr (kSage) {
-        // exp2 on packed halves: the f16 argument keeps ~1e-3 relative
-        // accuracy for |x| < 16, finer than the e4m3 P it feeds.
-        const float off = kLog2PScale - m_used;
+        const float off = (kLog2PScale - m_used) - 12582912.0f * comb;
+        uint32_t packed[16];  // 64 keys of e4m3 P = 16 TMEM columns
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float comb = c < 2 ? comb0 : comb1;
-          // f16x2 partial sums over 8 pairs each (<= 8 * 448), then fp32.
-          __half2 hsum0 = __float2half2_rn(0.f), hsum1 = hsum0;
+        for (int c = 0; c < 2; ++c) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
-            float x[4];
+            float x[4], pv[4];
+            ffma2(x[0], x[1], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb, off, off);
+            ffma2(x[2], x[3], __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]), comb, comb, off, off);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              x[t] = fmaf(static_cast<float>(static_cast<int>(r[c][e + t])), comb, off);
-              if (tail && c * 32 + e + t >= valid) x[t] = kNegInf;
-            }
-            const uint32_t e01 = ex2_f16x2(pack_f16x2(x[0], x[1]));
-            const uint32_t e23 = ex2_f16x2(pack_f16x2(x[2], x[3]));
-            hsum0 = __hadd2(hsum0, *reinterpret_cast<const __half2*>(&e01));
-            hsum1 = __hadd2(hsum1, *reinterpret_cast<const __half2*>(&e23));
-            packed[c * 8 + e / 4] = e4m3x2_from_f16x2(e01) | (e4m3x2_from_f16x2(e23) << 16);
+            for (int u = 0; u < 4; ++u)
+              pv[u] = use_poly(e + u) ? ex2_poly(x[u]) : ex2_approx(x[u]);
+            fadd2(rs0, rs1, rs0, rs1, pv[0], pv[1]);
+            fadd2(rs0, rs1, rs0, rs1, pv[2], pv[3]);
+            packed[c * 8 + e / 4] = pack_e4m3x2(pv[0], pv[1]) | (pack_e4m3x2(pv[2], pv[3]) << 16);
           }
-          const float2 f0 = __half22float2(hsum0), f1 = __half22float2(hsum1);
-          rs += (f0.x + f0.y) + (f1.x + f1.y);
         }
-        tmem_st32(s_addr, packed);
+        tmem_st16(s_addr, packed);
       } else {
         const float off = -m_used;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        for (int c = 0; c < 2; ++c) {
+          uint32_t packed[16];  // 32 keys of bf16 P = 16 TMEM columns
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const int col = (half * 2 + c) * 32 + e;
-              float xa = fmaf(__uint_as_float(r[half * 2 + c][e]), comb0, off);
-              float xb = fmaf(__uint_as_float(r[half * 2 + c][e + 1]), comb0, off);
-              if (tail) {
-                if (col >= valid) xa = kNegInf;
-                if (col + 1 >= valid) xb = kNegInf;
-              }
-              const float a = ex2_approx(xa);
-              const float b = ex2_approx(xb);
-              rs += a + b;
-              packed[c * 16 + e / 2] = pack_bf16x2(a, b);
-            }
+          for (int e = 0; e < 32; e += 2) {
+            float xa, xb;
+            ffma2(xa, xb, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb, off, off);
+            const float a = ex2_approx(xa);
+            const float b = use_poly(e + 1) ? ex2_poly(xb) : ex2_approx(xb);
+            fadd2(rs0, rs1, rs0, rs1, a, b);
+            packed[e / 2] = pack_bf16x2(a, b);
           }
-          tmem_st32(s_addr + half * 32, packed);
+          tmem_st16(s_addr + c * 16, packed);
         }
       }
-      l += rs;
+      mbar_arrive(&bars->turn[i ^ 1]);
+      l += rs0 + rs1;
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->p_full[i]);
+      mbar_arrive(&bars->p_full[i][t & 1]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full[i], 0, p.err));
+    // pv_done may trail the last tile by two phases here, so a parity wait
+    // on it would be ambiguous; o_done completes exactly once.
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[i], 0, p.err));
     if (ok) {
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.0f / l : 0.f;
@@ -456,6 +467,7 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, 
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
       cudaSuccess)
     return XGB_ERR_LAUNCH;
+
   dim3 grid(static_cast<unsigned>((p.seq_q + kQT * kBM - 1) / (kQT * kBM)),
             static_cast<unsigned>(bh));
   kernel<<<grid, kThreads, C::kSmem, st>>>(qm, km, vm, p);
@@ -496,10 +508,11 @@ XGB_API int xgb_attention_sage(const int8_t* q8, const float* q_scale, const int
   const uint64_t dims[3] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(s_pad),
                             static_cast<uint64_t>(bh)};
   const uint64_t strides[2] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(s_pad * kD)};
-  const uint32_t box[3] = {128, 128, 1};
-  if (!make_tensor_map(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, q8, dims, strides, box) ||
-      !make_tensor_map(&km, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, k8, dims, strides, box) ||
-      !make_tensor_map(&vm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, v8, dims, strides, box))
+  const uint32_t qbox[3] = {128, kBM, 1};
+  const uint32_t kvbox[3] = {128, kBN, 1};
+  if (!make_tensor_map(&qm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, q8, dims, strides, qbox) ||
+      !make_tensor_map(&km, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, k8, dims, strides, kvbox) ||
+      !make_tensor_map(&vm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, v8, dims, strides, kvbox))
     return XGB_ERR_ALIGN;
   Params p{};
   p.q_scale = q_scale;
@@ -540,16 +553,16 @@ XGB_API int xgb_attention_bf16(const void* q, const int64_t* q_strides, const vo
   int rc = check_device();
   if (rc) return rc;
   CUtensorMap qm, km, vm;
-  const uint32_t box[4] = {64, 128, 1, 1};
-  auto make = [&](CUtensorMap* m, const void* base, const int64_t* s, int64_t seq) {
+  auto make = [&](CUtensorMap* m, const void* base, const int64_t* s, int64_t seq, uint32_t rows) {
+    const uint32_t box[4] = {64, rows, 1, 1};
     const uint64_t dims[4] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(seq),
                               static_cast<uint64_t>(heads), static_cast<uint64_t>(batch)};
     const uint64_t strides[3] = {static_cast<uint64_t>(s[2]) * 2, static_cast<uint64_t>(s[1]) * 2,
                                  static_cast<uint64_t>(s[0]) * 2};
     return make_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box);
   };
-  if (!make(&qm, q, q_strides, seq_q) || !make(&km, k, k_strides, seq_kv) ||
-      !make(&vm, v, v_strides, seq_kv))
+  if (!make(&qm, q, q_strides, seq_q, kBM) || !make(&km, k, k_strides, seq_kv, kBN) ||
+      !make(&vm, v, v_strides, seq_kv, kBN))
     return XGB_ERR_ALIGN;
   Params p{};
   p.heads = static_cast<int>(heads);
