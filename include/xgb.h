@@ -126,6 +126,21 @@ int xgb_fp8_quantize_per_tensor(const void* x, int dtype, int64_t n, uint8_t* ou
                                 float* scale_out, void* workspace, int64_t workspace_bytes,
                                 void* stream);
 
+/* xgb_fp8_quantize_per_tensor for callers that cannot allocate device
+ * memory at call time (a plugin whose host runtime owns every allocation, a
+ * server that plans all of HBM up front, a latency-critical path that cannot
+ * take cudaMalloc's implicit device synchronisation). Same inputs, outputs
+ * and results as xgb_fp8_quantize_per_tensor, but the per-block peak scratch
+ * is a fixed 256 KiB array inside the library, so no workspace is passed and
+ * nothing is allocated. Limit: n <= 536,870,912 elements (65,536 peak
+ * blocks of 8,192); larger n returns XGB_ERR_SHAPE. The first call on each
+ * device resolves the array's device address (make it before any stream
+ * capture); every GPU that loads the library keeps the array until exit; all
+ * calls share it, so calls whose kernels overlap on one device race.
+ * No counterpart in the reference: it is an addition of this library. */
+int xgb_fp8_quantize_per_tensor_noalloc(const void* x, int dtype, int64_t n, uint8_t* out,
+                                        float* scale_out, void* stream);
+
 /* Per-token dynamic e4m3 (the per-token scaling of the B200 FP8 Linear):
  * scales[r] = max(amax(|x[r,:]|)/448, FLT_MIN), out[r,c] = e4m3(x/scale).
  * x rows strided by row_stride elements; out contiguous [rows, cols].

@@ -12,6 +12,7 @@
 // Per-token (the B200 FP8 Linear's activation scheme): the same formula per
 // row, computed by one warp per row.
 #include <cfloat>
+#include <mutex>
 
 #include "xgb_common.cuh"
 
@@ -199,5 +200,74 @@ XGB_API int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, i
   else
     per_token_kernel<<<grid, kThreads, 0, st>>>(static_cast<const __half*>(x), rows, cols,
                                                  row_stride, out, scales);
+  return launch_status();
+}
+
+// ---------------------------------------------------------------- no-allocation variant
+// Some callers of this library cannot allocate device memory at call time:
+// a plugin embedded in a host runtime that owns every device allocation and
+// hands out no workspace, a server that plans all of HBM up front and forbids
+// allocation while serving, or a latency-critical path that cannot afford
+// cudaMalloc's implicit device-wide synchronisation. For them,
+// xgb_fp8_quantize_per_tensor_noalloc takes the per-block peak scratch from
+// a fixed array compiled into the library instead of a caller workspace.
+//
+// The array is a file-scope __device__ symbol: every GPU that loads libxgb.so
+// holds its 256 KiB until the process exits. Its address is resolved once per
+// device (cudaGetSymbolAddress with that device current) on the entry point's
+// first call there, so that first call should come before any stream
+// capture. All calls share the one array and it keeps the last call's
+// contents; nothing needs clearing (each call writes every peak slot it later
+// reads), but calls whose kernels overlap on a device race on it.
+namespace xgb {
+namespace {
+
+constexpr int64_t kNoAllocMaxBlocks = 65536;  // peaks of 65536 x 8192 elements
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) int g_noalloc_peaks[kNoAllocMaxBlocks];
+
+std::mutex g_noalloc_mutex;
+int* g_noalloc_scratch[kMaxDevices] = {};
+
+int noalloc_scratch(int** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return XGB_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch[dev] == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_noalloc_peaks) != cudaSuccess || addr == nullptr)
+      return XGB_ERR_LAUNCH;
+    g_noalloc_scratch[dev] = static_cast<int*>(addr);
+  }
+  *out = g_noalloc_scratch[dev];
+  return XGB_OK;
+}
+
+}  // namespace
+}  // namespace xgb
+
+XGB_API int xgb_fp8_quantize_per_tensor_noalloc(const void* x, int dtype, int64_t n, uint8_t* out,
+                                                float* scale_out, void* stream) {
+  if (!x || !out || !scale_out) return XGB_ERR_ARG;
+  if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
+  if (n <= 0 || cdiv(n, kPeakBlock) > kNoAllocMaxBlocks) return XGB_ERR_SHAPE;
+  int* peaks = nullptr;
+  const int rc = noalloc_scratch(&peaks);
+  if (rc != XGB_OK) return rc;
+  const int64_t blocks = cdiv(n, kPeakBlock);
+  cudaStream_t st = as_stream(stream);
+  const unsigned pack_grid = static_cast<unsigned>(cdiv(cdiv(n, 8), kThreads));
+  if (dtype == XGB_BF16) {
+    auto xb = static_cast<const __nv_bfloat16*>(x);
+    abs_peak_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(xb, n, peaks);
+    peak_to_scale_kernel<<<1, kThreads, 0, st>>>(peaks, blocks, scale_out);
+    pack_kernel<<<pack_grid, kThreads, 0, st>>>(xb, n, scale_out, out);
+  } else {
+    auto xh = static_cast<const __half*>(x);
+    abs_peak_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(xh, n, peaks);
+    peak_to_scale_kernel<<<1, kThreads, 0, st>>>(peaks, blocks, scale_out);
+    pack_kernel<<<pack_grid, kThreads, 0, st>>>(xh, n, scale_out, out);
+  }
   return launch_status();
 }
