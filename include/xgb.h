@@ -149,6 +149,27 @@ int xgb_fp8_quantize_per_tensor_noalloc(const void* x, int dtype, int64_t n, uin
 int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, int64_t cols,
                                int64_t row_stride, uint8_t* out, float* scales, void* stream);
 
+/* ---- FP8 GEMM (tcgen05 kind::f8f6f4) ---- */
+
+/* out[m, n] = bf16(acc[m, n] * (scale_a[m*sa_stride] * scale_w[n*sw_stride])
+ *                  + bias[n])
+ * with acc = sum_k a[m, k] * w[n, k] in fp32; a [M, K] and w [N, K] e4m3
+ * row-major (16-byte aligned, K and N multiples of 16); scale strides 0
+ * (per-tensor scalar) or 1 (per row / per output channel); bias bf16 [N]
+ * or NULL; out bf16 rows ldo elements apart.
+ * When gate != NULL the AdaLN gated residual is fused in, with the
+ * reference's rounding after each op:
+ *     out[m, n] = bf16(bf16(y * gate[gate_index[m]*ldg + n]) + residual[m*ldr + n])
+ * error_flag as for the attention kernels.
+ * Replaces torch._scaled_mm in H3FP8Linear._local_forward
+ * (x_base/x_base/operator/h3_fp8.py:48-68) and the gated `_apply` after the
+ * output projections (x_base/x_base/operator/h3_indexed_affine.py:52-61). */
+int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t N, int64_t K,
+                 const float* scale_a, int64_t scale_a_stride, const float* scale_w,
+                 int64_t scale_w_stride, const void* bias, void* out, int64_t ldo,
+                 const void* gate, int64_t ldg, const int64_t* gate_index, const void* residual,
+                 int64_t ldr, int* error_flag, void* stream);
+
 /* ---- Attention (tcgen05 / TMEM / TMA kernels) ---- */
 
 /* Bytes of workspace xgb_sage_prepare needs. */

@@ -1,0 +1,104 @@
+"""tcgen05 FP8 GEMM / H3FP8Linear vs torch._scaled_mm, the CPU oracle and
+the reference's own accuracy bound.
+
+Tolerance: the GEMM's fp32 accumulation order differs from cuBLASLt's and
+from the oracle's exact sum, so bf16 outputs may differ by one bf16 ulp at
+a rounding boundary: we require <= 1 ulp everywhere and >= 99.5 % identical."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import fp8 as of
+from oracle.numerics import bf16_bits_from_f32
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> np.ndarray:
+    ai = a.contiguous().cpu().view(torch.int16).numpy().astype(np.int32)
+    bi = b.contiguous().cpu().view(torch.int16).numpy().astype(np.int32)
+    return np.abs(ai - bi)
+
+
+def test_fp8_projection_bias_and_unaligned_rows(cuda_device):
+    """x_base/tests/test_h3_cuda_precision_ops.py:19-32 on our module."""
+    from xgen_b200.fp8_linear import H3FP8Linear
+
+    torch.manual_seed(42)
+    weight = torch.randn(256, 128, dtype=torch.bfloat16)
+    bias = torch.randn(256, dtype=torch.bfloat16)
+    layer = H3FP8Linear(weight, bias).cuda()
+    x = torch.randn(2, 19, 128, device=cuda_device, dtype=torch.bfloat16)
+    result = layer(x)
+    reference = torch.nn.functional.linear(x, weight.cuda(), bias.cuda())
+    assert result.shape == reference.shape and result.dtype == reference.dtype
+    assert layer.weight.dtype == torch.float8_e4m3fn and layer.calls == 1
+    assert torch.isfinite(result).all()
+    rel = (result.float() - reference.float()).square().mean().sqrt() / reference.float().square().mean().sqrt()
+    assert rel.item() < 0.08
+
+
+def test_projection_rejects_unaligned_dimensions():
+    from xgen_b200.fp8_linear import H3FP8Linear
+
+    with pytest.raises(ValueError, match="divisible by 16"):
+        H3FP8Linear(torch.randn(17, 32))
+
+
+@pytest.mark.parametrize("m,n,k", [(19, 256, 128), (1000, 3072, 3072), (333, 9216, 3072),
+                                   (64, 12288, 3072), (130, 3072, 12288)])
+def test_per_tensor_gemm_matches_scaled_mm(cuda_device, m, n, k):
+    from xgen_b200.fp8_linear import H3FP8Linear
+
+    g = torch.Generator().manual_seed(m + n)
+    w = (torch.randn(n, k, generator=g) * 0.02).bfloat16()
+    bias = torch.randn(n, generator=g).bfloat16()
+    layer = H3FP8Linear(w, bias).to(cuda_device)
+    x = torch.randn(m, k, generator=g).bfloat16().to(cuda_device)
+    got = layer(x)
+    from xgen_b200.ops import quantize_activation
+
+    qa, sa = quantize_activation(x)
+    ref = torch._scaled_mm(qa, layer.weight.t(), scale_a=sa, scale_b=layer.weight_scale.reshape(()),
+                           bias=layer.bias, out_dtype=torch.bfloat16)
+    d = ulp_diff(got, ref)
+    assert d.max() <= 1 and (d == 0).mean() >= 0.995
+
+
+def test_per_token_gemm_matches_oracle(cuda_device):
+    from xgen_b200.fp8_linear import H3FP8Linear
+
+    g = torch.Generator().manual_seed(3)
+    m, n, k = 200, 1024, 3072
+    w = (torch.randn(n, k, generator=g) * 0.02).bfloat16()
+    layer = H3FP8Linear(w, None, scaling="per_token").to(cuda_device)
+    x = (torch.randn(m, k, generator=g) * torch.rand(m, 1, generator=g) * 5).bfloat16().to(cuda_device)
+    got = layer(x)
+    qa, sa = of.quantize_per_token(x.float().cpu().numpy())
+    qw = layer.weight.view(torch.uint8).cpu().numpy()
+    sw = layer.weight_scale.cpu().numpy()
+    ref = of.scaled_mm(qa, qw, sa, sw)
+    d = np.abs(got.cpu().view(torch.int16).numpy().astype(np.int32) -
+               bf16_bits_from_f32(ref).view(np.int16).astype(np.int32))
+    assert d.max() <= 1 and (d == 0).mean() >= 0.995
+
+
+def test_gated_epilogue_matches_gemm_then_indexed_affine(cuda_device):
+    """attn_out -> x + gate[idx] * attn_out with the reference's rounding,
+    fused vs GEMM followed by the (bit-exact) indexed-affine kernel."""
+    from xgen_b200.fp8_linear import H3FP8Linear
+    from xgen_b200.ops import indexed_affine
+
+    g = torch.Generator().manual_seed(9)
+    b, s, hid = 1, 333, 3072
+    w = (torch.randn(hid, hid, generator=g) * 0.02).bfloat16()
+    layer = H3FP8Linear(w, torch.randn(hid, generator=g).bfloat16(), scaling="per_token").to(cuda_device)
+    x = torch.randn(b, s, hid, generator=g).bfloat16().to(cuda_device)
+    res = torch.randn(b, s, hid, generator=g).bfloat16().to(cuda_device)
+    tables = torch.randn(3, 6 * hid, generator=g).bfloat16().to(cuda_device)
+    gate = tables[:, 2 * hid:3 * hid]
+    idx = torch.randint(3, (s,), generator=g).to(cuda_device)
+    fused = layer.forward_gated(x, gate, idx, res)
+    plain = layer(x)
+    two_step = indexed_affine(plain, gate, res, idx, modulation=False)
+    assert torch.equal(fused, two_step)

@@ -373,7 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // P = exp2(comb*s - m_used) (times kPScale for e4m3, folded into the
       // exponent), row sum, pack and store over the S buffer.
-      float rs0 = 0.f, rs1 = 0.f;
+      // Row sums in four independent packed chains (short dependency chains).
+      float rsa[4] = {0.f, 0.f, 0.f, 0.f}, rsb[4] = {0.f, 0.f, 0.f, 0.f};
       if constexpr (kSage) {
         const float off = (kLog2PScale - m_used) - 12582912.0f * comb;
         uint32_t packed[16];  // 64 keys of e4m3 P = 16 TMEM columns
@@ -387,8 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 4; ++u)
               pv[u] = use_poly(e + u) ? ex2_poly(x[u]) : ex2_approx(x[u]);
-            fadd2(rs0, rs1, rs0, rs1, pv[0], pv[1]);
-            fadd2(rs0, rs1, rs0, rs1, pv[2], pv[3]);
+            const int ch = (e / 4) & 1;
+            fadd2(rsa[2 * ch], rsb[2 * ch], rsa[2 * ch], rsb[2 * ch], pv[0], pv[1]);
+            fadd2(rsa[2 * ch + 1], rsb[2 * ch + 1], rsa[2 * ch + 1], rsb[2 * ch + 1], pv[2], pv[3]);
             packed[c * 8 + e / 4] = pack_e4m3x2(pv[0], pv[1]) | (pack_e4m3x2(pv[2], pv[3]) << 16);
           }
         }
@@ -404,14 +406,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             ffma2(xa, xb, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb, off, off);
             const float a = ex2_approx(xa);
             const float b = use_poly(e + 1) ? ex2_poly(xb) : ex2_approx(xb);
-            fadd2(rs0, rs1, rs0, rs1, a, b);
+            const int ch = (e / 2) & 3;
+            fadd2(rsa[ch], rsb[ch], rsa[ch], rsb[ch], a, b);
             packed[e / 2] = pack_bf16x2(a, b);
           }
           tmem_st16(s_addr + c * 16, packed);
         }
       }
       mbar_arrive(&bars->turn[i ^ 1]);
-      l += rs0 + rs1;
+      l += ((rsa[0] + rsb[0]) + (rsa[1] + rsb[1])) + ((rsa[2] + rsb[2]) + (rsa[3] + rsb[3]));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->p_full[i][t & 1]);

@@ -1,0 +1,298 @@
+// FP8 (e4m3) GEMM on sm_100a tensor cores for the H3 FP8 Linear layers.
+//
+//   out[m, n] = bf16(acc[m, n] * (sa[m] * sb[n]) + bias[n])        (plain)
+//   out[m, n] = bf16(bf16(y * gate[idx[m], n]) + residual[m, n])    (gated)
+//       with y = the plain result, the AdaLN gate + residual of the block
+//
+// acc = sum_k A[m, k] * W[n, k] in fp32 (tcgen05 kind::f8f6f4), A [M, K] and
+// W [N, K] e4m3 row-major (both K-major), sa/sb per-row/per-column scales
+// or broadcast scalars (stride 0), bias optional. Replaces torch._scaled_mm
+// in H3FP8Linear._local_forward (x_base/x_base/operator/h3_fp8.py:48-68) and,
+// in the gated form, the `_apply(..., modulation=False)` that follows the
+// attention/FFN output projections (x_base/x_base/operator/h3_indexed_affine.py
+// :52-61), with the reference's rounding after each eager op.
+//
+// Persistent kernel, one CTA per SM, tiles of 128 x 256 (M x N), K blocks
+// of 128 bytes:
+//   warp 0     TMA producer (A 16 KB + W 32 KB per stage, 4 stages)
+//   warp 1     TMEM allocator + MMA issuer (4 x M128 N256 K32 per stage)
+//   warps 2-5  epilogue: one thread per output row (TMEM lane), 256 fp32
+//              columns read in chunks of 32
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile run
+// under the MMAs of the next. Every mbarrier wait is bounded.
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace xgb {
+namespace gemm {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 128;  // bytes of K per stage (e4m3)
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kABytes = kBM * kBK;
+constexpr int kBBytes = kBN * kBK;
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kBarOff = kStages * kStageBytes;
+constexpr int kSmem = kBarOff + 256 + 1024;
+constexpr uint32_t kIdesc = instr_desc(1, 0, 0, false, false, kBM, kBN);
+
+enum Epilogue : int { kPlain = 0, kGated = 1 };
+
+struct Params {
+  int M, N, K;
+  const float* sa;
+  int64_t sa_stride;  // 0: per-tensor scalar, 1: per row
+  const float* sb;
+  int64_t sb_stride;  // 0: per-tensor scalar, 1: per column
+  const __nv_bfloat16* bias;  // may be null
+  __nv_bfloat16* out;
+  int64_t ldo;
+  // gated epilogue
+  const __nv_bfloat16* gate;  // rows of the AdaLN table, row stride ldg
+  int64_t ldg;
+  const int64_t* idx;         // [M] table row of each output row
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  int* err;
+};
+
+struct Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t end;
+  uint32_t tmem_base;
+};
+
+template <int kEpi>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap a_map,
+                    const __grid_constant__ CUtensorMap b_map, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kBarOff);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (p.M + kBM - 1) / kBM;
+  const int n_tiles = (p.N + kBN - 1) / kBN;
+  const int tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 128);
+    }
+    mbar_init(&bars->end, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc<512>(&bars->tmem_base);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&a_map);
+    prefetch_tmap(&b_map);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      bool ok = true;
+      int it = 0;  // global k-block counter of this CTA
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m0 = (t / n_tiles) * kBM;
+        const int n0 = (t % n_tiles) * kBN;
+        for (int kb = 0; kb < k_blocks && ok; ++kb, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages) ok = mbar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, p.err);
+          if (!ok) break;
+          uint8_t* st = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+          tma_load_2d(st, &a_map, &bars->full[s], kb * kBK, m0);
+          tma_load_2d(st + kABytes, &b_map, &bars->full[s], kb * kBK, n0);
+        }
+      }
+      // drain: the last stages' copies must land before the CTA exits
+      for (int j = max(0, it - kStages); j < it; ++j)
+        mbar_wait(&bars->full[j % kStages], (j / kStages) & 1, p.err, 100000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      int it = 0, lt = 0;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++lt) {
+        const int a = lt & 1;
+        if (lt >= 2) ok = mbar_wait(&bars->acc_empty[a], ((lt >> 1) - 1) & 1, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + a * kBN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          ok = mbar_wait(&bars->full[s], (it / kStages) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t as = smem_u32(smem + s * kStageBytes);
+          const uint32_t bs = as + kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            mma_ss<Kind::kF8F6F4>(d, smem_desc_sw128(as + k * 32, 16, 1024),
+                                  smem_desc_sw128(bs + k * 32, 16, 1024), kIdesc, kb > 0 || k > 0);
+          tc_commit(&bars->empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&bars->acc_full[a]);
+      }
+      tc_commit(&bars->end);
+      mbar_wait(&bars->end, 0, p.err, 100000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    int lt = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+      const int a = lt & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[a], (lt >> 1) & 1, p.err));
+      if (!ok) break;
+      tc_fence_after();
+      const int m = (t / n_tiles) * kBM + quarter * 32 + lane;
+      const int n0 = (t % n_tiles) * kBN;
+      const bool row_ok = m < p.M;
+      const float sa = row_ok ? p.sa[m * p.sa_stride] : 0.f;
+      const int64_t grow = (kEpi == kGated && row_ok) ? p.idx[m] : 0;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(lane_addr + a * kBN + c * 32, r);
+        tmem_ld_wait();
+        const int nb = n0 + c * 32;
+        if (row_ok && nb < p.N) {
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float y[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int n = min(nb + e + u, p.N - 1);
+              const float alpha = sa * p.sb[n * p.sb_stride];
+              const float bias = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+              y[u] = fmaf(__uint_as_float(r[e + u]), alpha, bias);
+              if constexpr (kEpi == kGated) {
+                // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
+                const float g = __bfloat162float(p.gate[grow * p.ldg + n]);
+                const float res = __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + n]);
+                y[u] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[u]), g)), res);
+              }
+            }
+            w[e / 2] = pack_bf16x2(y[0], y[1]);
+          }
+          __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
+          if (nb + 32 <= p.N) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+          } else {
+            const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+            for (int e = 0; e < p.N - nb; ++e) dst[e] = wb[e];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty[a]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int kEpi>
+int launch(const void* a, const void* w, const Params& p, cudaStream_t st) {
+  CUtensorMap am, bm;
+  const uint64_t adims[2] = {static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M)};
+  const uint64_t astr[1] = {static_cast<uint64_t>(p.K)};
+  const uint32_t abox[2] = {kBK, kBM};
+  const uint64_t bdims[2] = {static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N)};
+  const uint32_t bbox[2] = {kBK, kBN};
+  if (!make_tensor_map(&am, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, adims, astr, abox) ||
+      !make_tensor_map(&bm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, bdims, astr, bbox))
+    return XGB_ERR_ALIGN;
+  auto kernel = gemm_fp8_kernel<kEpi>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+    return XGB_ERR_LAUNCH;
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + kBN - 1) / kBN);
+  const int grid = std::min(tiles, sm_count());
+  kernel<<<grid, kThreads, kSmem, st>>>(am, bm, p);
+  return launch_status();
+}
+
+}  // namespace gemm
+}  // namespace xgb
+
+using namespace xgb;
+
+XGB_API int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t N, int64_t K,
+                         const float* scale_a, int64_t scale_a_stride, const float* scale_w,
+                         int64_t scale_w_stride, const void* bias, void* out, int64_t ldo,
+                         const void* gate, int64_t ldg, const int64_t* gate_index,
+                         const void* residual, int64_t ldr, int* error_flag, void* stream) {
+  if (!a || !w || !scale_a || !scale_w || !out) return XGB_ERR_ARG;
+  if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return XGB_ERR_SHAPE;
+  if (K % 16 || N % 16) return XGB_ERR_SHAPE;  // 16-byte TMA rows, as the reference requires
+  if ((scale_a_stride != 0 && scale_a_stride != 1) || (scale_w_stride != 0 && scale_w_stride != 1))
+    return XGB_ERR_STRIDE;
+  if (ldo < N || ldo % 8) return XGB_ERR_STRIDE;
+  const bool gated = gate != nullptr;
+  if (gated && (!gate_index || !residual || ldr < N || ldg < N)) return XGB_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) |
+       reinterpret_cast<uintptr_t>(out)) & 15u)
+    return XGB_ERR_ALIGN;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      major != 10)
+    return XGB_ERR_DEVICE;
+  gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.sa = scale_a;
+  p.sa_stride = scale_a_stride;
+  p.sb = scale_w;
+  p.sb_stride = scale_w_stride;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.ldg = ldg;
+  p.idx = gate_index;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.ldr = ldr;
+  p.err = error_flag;
+  cudaStream_t st = as_stream(stream);
+  return gated ? gemm::launch<gemm::kGated>(a, w, p, st) : gemm::launch<gemm::kPlain>(a, w, p, st);
+}

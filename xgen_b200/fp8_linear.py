@@ -1,0 +1,134 @@
+"""FP8 Linear on the B200 tcgen05 GEMM.
+
+Mirror of H3FP8Linear (x_base/x_base/operator/h3_fp8.py:15-68): e4m3
+weights with an fp32 scale, dynamic e4m3 activations, bf16 output with an
+optional bias, the same construction checks (dimensions divisible by 16)
+and forward checks (CUDA bf16/fp16 input of the right width). Two scaling
+schemes:
+
+  "per_tensor"  the reference's: one weight scale, one activation scale per
+                call (abs-peak / 448, evaluated with CUDA semantics)
+  "per_token"   B200 target: per-output-channel weight scales and per-token
+                activation scales
+
+`forward_gated` fuses the AdaLN gated residual that follows the attention and
+FFN output projections (h3_indexed_affine.py:52-61) into the GEMM epilogue.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import _lib
+from ._lib import call
+from .ops import quantize_activation, quantize_per_token
+
+
+def quantize_per_tensor(value: torch.Tensor):
+    """(e4m3 tensor, fp32 scale) with scale = max(amax/448, FLT_MIN), as
+    x_base/x_base/operator/h3_fp8.py:9-12 on the tensor's own device."""
+    maximum = torch.finfo(torch.float8_e4m3fn).max
+    scale = (value.float().abs().amax() / maximum).clamp_min(torch.finfo(torch.float32).tiny)
+    return (value.float() / scale).clamp(-maximum, maximum).to(torch.float8_e4m3fn), scale
+
+
+def quantize_per_channel(value: torch.Tensor):
+    """Per-row (output channel) e4m3 of a [out, in] weight."""
+    maximum = torch.finfo(torch.float8_e4m3fn).max
+    scale = (value.float().abs().amax(dim=1) / maximum).clamp_min(torch.finfo(torch.float32).tiny)
+    return (value.float() / scale[:, None]).clamp(-maximum, maximum).to(torch.float8_e4m3fn), scale
+
+
+class H3FP8Linear(nn.Module):
+    """Keep FP8 weights; quantise activations to e4m3 on every call."""
+
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                 scaling: str = "per_tensor"):
+        super().__init__()
+        if weight.ndim != 2 or weight.shape[0] % 16 or weight.shape[1] % 16:
+            raise ValueError("H3 FP8 requires projection dimensions divisible by 16")
+        if scaling not in ("per_tensor", "per_token"):
+            raise ValueError(f"Unknown FP8 scaling: {scaling}")
+        self.scaling = scaling
+        self.out_features, self.in_features = weight.shape
+        packed, scale = (quantize_per_tensor if scaling == "per_tensor" else quantize_per_channel)(
+            weight.detach())
+        self.register_buffer("weight", packed.contiguous())
+        self.register_buffer("weight_scale", scale.reshape(-1).float())
+        self.register_buffer("bias", bias.detach().clone().to(torch.bfloat16) if bias is not None else None)
+        self.calls = 0
+
+    @classmethod
+    def from_packed(cls, weight, scale, bias=None):
+        """Reuse quantised bytes and their scale (h3_fp8.py:26-39)."""
+        if weight.dtype != torch.float8_e4m3fn or weight.ndim != 2 or any(n % 16 for n in weight.shape):
+            raise ValueError("Packed H3 FP8 projection requires an aligned E4M3 matrix")
+        if scale.numel() != 1 or scale.dtype != torch.float32:
+            raise ValueError("Packed H3 FP8 projection requires one FP32 weight scale")
+        result = cls.__new__(cls)
+        nn.Module.__init__(result)
+        result.scaling = "per_tensor"
+        result.out_features, result.in_features = weight.shape
+        result.register_buffer("weight", weight.contiguous())
+        result.register_buffer("weight_scale", scale.detach().clone().reshape(1))
+        result.register_buffer("bias", bias.detach().clone().to(torch.bfloat16) if bias is not None else None)
+        result.calls = 0
+        return result
+
+    def _check(self, x):
+        if not x.is_cuda or x.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("H3 FP8 Linear requires CUDA BF16/FP16 input")
+        if x.shape[-1] != self.in_features:
+            raise ValueError("H3 FP8 Linear input width does not match its weight")
+
+    def _quantize(self, matrix):
+        if self.scaling == "per_tensor":
+            q, s = quantize_activation(matrix)
+            return q, s.reshape(1), 0
+        q, s = quantize_per_token(matrix)
+        return q, s, 1
+
+    def forward(self, x):
+        return self._forward(x, None)
+
+    def forward_gated(self, x, gate_table, gate_index, residual):
+        """residual + gate_table[gate_index] * self(x), each eager op rounded
+        to bf16 (the block's `_apply(..., modulation=False)`), in one GEMM."""
+        if (gate_table.dtype != torch.bfloat16 or gate_table.stride(-1) != 1
+                or gate_table.shape[-1] != self.out_features or residual.dtype != torch.bfloat16
+                or residual.shape[-1] != self.out_features or residual.stride(-1) != 1):
+            raise ValueError("gated FP8 Linear needs bf16 gate rows [.., out] and a bf16 residual")
+        return self._forward(x, (gate_table, gate_index, residual))
+
+    def _forward(self, x, gated):
+        self._check(x)
+        matrix = x.reshape(-1, self.in_features)
+        m = matrix.shape[0]
+        if not m:
+            return x.new_empty((*x.shape[:-1], self.out_features))
+        matrix = matrix.contiguous()
+        q, sa, sa_stride = self._quantize(matrix)
+        out = torch.empty((m, self.out_features), device=x.device, dtype=torch.bfloat16)
+        gate = idx = res = None
+        ldg = ldr = 0
+        if gated is not None:
+            gate, idx, res = gated
+            res = res.reshape(-1, self.out_features)
+            idx = idx.reshape(-1)
+            if idx.numel() != m:  # indices over the sequence, broadcast over batch
+                idx = idx.repeat(m // idx.numel())
+            idx = idx.to(torch.int64).contiguous()
+            ldg, ldr = gate.stride(0), res.stride(0)
+        from .attention import _err_flag
+
+        call("xgb_fp8_gemm", q.data_ptr(), self.weight.data_ptr(), m, self.out_features,
+             self.in_features, sa.data_ptr(), sa_stride, self.weight_scale.data_ptr(),
+             0 if self.weight_scale.numel() == 1 else 1,
+             self.bias.data_ptr() if self.bias is not None else None, out.data_ptr(),
+             self.out_features, gate.data_ptr() if gate is not None else None, ldg,
+             idx.data_ptr() if idx is not None else None,
+             res.data_ptr() if res is not None else None, ldr, _err_flag(x.device).data_ptr(),
+             torch.cuda.current_stream(x.device).cuda_stream)
+        self.calls += 1
+        out = out.reshape(*x.shape[:-1], self.out_features)
+        return out if x.dtype == torch.bfloat16 else out.to(x.dtype)
