@@ -58,7 +58,49 @@ def parse():
                     help="time only the attention kernel on --seq/--heads (profiling case)")
     ap.add_argument("--seq", type=int, default=SEQ)
     ap.add_argument("--heads", type=int, default=HEADS)
+    ap.add_argument("--linear-only", action="store_true",
+                    help="time the FP8 Linear stack of one block (BASELINE config 4)")
+    ap.add_argument("--sp", type=int, default=8, help="SP degree that sets the linear-stack M")
     return ap.parse_args()
+
+
+def linear_stack(args, dev=None, quiet=False):
+    """the block's FP8 Linear stack (QKV hid->3*hid, O,
+    FFN up hid->F, down F->hid) at M = ceil(126,754 / sp) tokens, per-token
+    e4m3 activations and per-channel e4m3 weights; times each projection
+    (activation quantisation + tcgen05 GEMM) with CUDA events."""
+    import torch
+
+    from xgen_b200.fp8_linear import H3FP8Linear
+
+    dev = dev or torch.device("cuda", 0)
+    hid, ffn = 3072, 12288
+    m = -(-SEQ // max(1, args.sp))
+    g = torch.Generator(device=dev).manual_seed(3)
+    shapes = {"to_qkv": (3 * hid, hid), "to_out": (hid, hid), "ff_up": (ffn, hid), "ff_down": (hid, ffn)}
+    res, total_flops, total_ms = {}, 0.0, 0.0
+    for name, (n, k) in shapes.items():
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+        layer = H3FP8Linear(w, torch.zeros(n, device=dev, dtype=torch.bfloat16), scaling="per_token")
+        x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+        for _ in range(max(1, args.warmup)):
+            layer(x)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            layer(x)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / args.steps
+        flops = 2.0 * m * n * k
+        res[name] = {"ms": ms, "tflops": flops / ms / 1e9}
+        total_flops += flops
+        total_ms += ms
+    out = {"linear_stack": res, "m": m, "total_ms": total_ms, "tflops": total_flops / total_ms / 1e9}
+    if not quiet:
+        print(json.dumps(out), flush=True)
+    return out
 
 
 def kernel_only(args):
@@ -226,6 +268,8 @@ def main():
         return run_reference(args)
     if args.kernel_only:
         return kernel_only(args)
+    if args.linear_only:
+        return linear_stack(args)
 
     import torch
     import torch.distributed as dist

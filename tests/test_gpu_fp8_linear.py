@@ -2,22 +2,31 @@
 the reference's own accuracy bound.
 
 Tolerance: the GEMM's fp32 accumulation order differs from cuBLASLt's and
-from the oracle's exact sum, so bf16 outputs may differ by one bf16 ulp at
-a rounding boundary: we require <= 1 ulp everywhere and >= 99.5 % identical."""
+from the oracle's exact sum. Where an output cancels towards zero, that
+fp32 difference (about K * 2^-24 * |terms|) can be a few ulps of the small
+bf16 result, so the bound is relative to the output scale: >= 99.5 % of
+elements bit-identical and |difference| <= 2^-10 * rms(reference) everywhere."""
 import numpy as np
 import pytest
 import torch
 
 from oracle import fp8 as of
-from oracle.numerics import bf16_bits_from_f32
 
 pytestmark = pytest.mark.gpu
 
 
-def ulp_diff(a: torch.Tensor, b: torch.Tensor) -> np.ndarray:
-    ai = a.contiguous().cpu().view(torch.int16).numpy().astype(np.int32)
-    bi = b.contiguous().cpu().view(torch.int16).numpy().astype(np.int32)
-    return np.abs(ai - bi)
+def assert_gemm_close(got: torch.Tensor, ref) -> None:
+    """Per element: |got - ref| <= one bf16 ulp of |ref| + 2^-10 * rms(ref)
+    (the cancellation allowance), and >= 99.5 % of elements identical."""
+    g = got.float().cpu().numpy().astype(np.float64)
+    r = ref.float().cpu().numpy() if isinstance(ref, torch.Tensor) else np.asarray(ref, np.float32)
+    r = r.astype(np.float64)
+    rms = np.sqrt((r ** 2).mean())
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(r), 1e-30))) - 7)
+    bound = ulp + 2.0 ** -10 * rms
+    worst = (np.abs(g - r) / bound).max()
+    same = (g == r).mean()
+    assert same >= 0.995 and worst <= 1.0, (same, worst)
 
 
 def test_fp8_projection_bias_and_unaligned_rows(cuda_device):
@@ -61,8 +70,7 @@ def test_per_tensor_gemm_matches_scaled_mm(cuda_device, m, n, k):
     qa, sa = quantize_activation(x)
     ref = torch._scaled_mm(qa, layer.weight.t(), scale_a=sa, scale_b=layer.weight_scale.reshape(()),
                            bias=layer.bias, out_dtype=torch.bfloat16)
-    d = ulp_diff(got, ref)
-    assert d.max() <= 1 and (d == 0).mean() >= 0.995
+    assert_gemm_close(got, ref)
 
 
 def test_per_token_gemm_matches_oracle(cuda_device):
@@ -78,9 +86,7 @@ def test_per_token_gemm_matches_oracle(cuda_device):
     qw = layer.weight.view(torch.uint8).cpu().numpy()
     sw = layer.weight_scale.cpu().numpy()
     ref = of.scaled_mm(qa, qw, sa, sw)
-    d = np.abs(got.cpu().view(torch.int16).numpy().astype(np.int32) -
-               bf16_bits_from_f32(ref).view(np.int16).astype(np.int32))
-    assert d.max() <= 1 and (d == 0).mean() >= 0.995
+    assert_gemm_close(got, ref)
 
 
 def test_gated_epilogue_matches_gemm_then_indexed_affine(cuda_device):
