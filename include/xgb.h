@@ -156,7 +156,8 @@ int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, int64_t c
  * with acc = sum_k a[m, k] * w[n, k] in fp32; a [M, K] and w [N, K] e4m3
  * row-major (16-byte aligned, K and N multiples of 16); scale strides 0
  * (per-tensor scalar) or 1 (per row / per output channel); bias bf16 [N]
- * or NULL; out bf16 rows ldo elements apart.
+ * or NULL; out bf16 rows ldo elements apart. activation: 0 none, 1 GELU
+ * (erf), 2 GELU (tanh approximation), applied after the bias (FFN up).
  * When gate != NULL the AdaLN gated residual is fused in, with the
  * reference's rounding after each op:
  *     out[m, n] = bf16(bf16(y * gate[gate_index[m]*ldg + n]) + residual[m*ldr + n])
@@ -166,9 +167,26 @@ int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, int64_t c
  * output projections (x_base/x_base/operator/h3_indexed_affine.py:52-61). */
 int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t N, int64_t K,
                  const float* scale_a, int64_t scale_a_stride, const float* scale_w,
-                 int64_t scale_w_stride, const void* bias, void* out, int64_t ldo,
+                 int64_t scale_w_stride, const void* bias, int activation, void* out, int64_t ldo,
                  const void* gate, int64_t ldg, const int64_t* gate_index, const void* residual,
                  int64_t ldr, int* error_flag, void* stream);
+
+/* AdaLN prologue of an FP8 Linear, one HBM pass per row of x [rows, width]
+ * (rows = batch * seq, row stride ldx):
+ *   n = norm(x) rounded to bf16, norm_kind 0 = LayerNorm without affine,
+ *       1 = RMSNorm times the bf16 weight (weight may be NULL), eps
+ *   h = bf16(bf16(n * bf16(1 + scale[t])) + shift[t]),  t = indices[row % seq]
+ *   out = e4m3(h / s), out_scale[row] = s = max(amax|h| / 448, FLT_MIN)
+ * scale/shift are bf16 table rows (strides lds/ldsh); out_bf16 (optional)
+ * receives h. width <= 6144.
+ * Replaces norm1/norm2 + `_apply(..., modulation=True)` of the H3 block
+ * (x_base/x_base/operator/h3_indexed_affine.py:52-61,
+ * x_diffusers/x_diffusers/framework/transformer/h3_npu_fusion.py:339-356)
+ * plus the next FP8 Linear's activation quantisation. */
+int xgb_norm_modulate_quant(const void* x, int64_t ldx, int64_t rows, int64_t width, int64_t seq,
+                            int norm_kind, const void* weight, float eps, const void* scale,
+                            int64_t lds, const void* shift, int64_t ldsh, const int64_t* indices,
+                            uint8_t* out, float* out_scale, void* out_bf16, void* stream);
 
 /* ---- Attention (tcgen05 / TMEM / TMA kernels) ---- */
 

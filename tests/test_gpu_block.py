@@ -1,0 +1,74 @@
+"""The H3 DiT block on B200 kernels (FP8 linears, Sage/BF16 attention,
+fused AdaLN) vs the fp32 restatement of the reference block math.
+
+Tolerance: FP8 e4m3 projections carry ~3-5 % relative error each (the
+reference's own FP8-vs-BF16 bound is rel-RMSE < 0.08 per projection,
+x_base/tests/test_h3_cuda_precision_ops.py:19-32). The block's branch
+output (y - x) must keep cosine >= 0.99 with the fp32 branch, and the fused
+prologue must agree with the unfused kernels it replaces."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import block as ob
+from oracle.attention import cosine
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(cfg, s, seed=0):
+    from xgen_b200.h3.block import H3DiTBlockB200
+    from xgen_b200.h3.rope import rope_partial
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(1, s, cfg.hidden, generator=g).bfloat16()
+    table = (0.5 * torch.randn(3, 6 * cfg.hidden, generator=g)).bfloat16()
+    idx = torch.randint(3, (s,), generator=g)
+    cos, sin = rope_partial(s, 96)
+    w = H3DiTBlockB200.random_weights(cfg, seed)
+    return x, table, idx, cos, sin, w
+
+
+@pytest.mark.parametrize("variant", ["baseline", "reference_model"])
+@pytest.mark.parametrize("precision", ["sage", "bf16"])
+def test_block_vs_fp32_restatement(cuda_device, variant, precision):
+    from xgen_b200.h3.block import H3BlockConfig, H3DiTBlockB200
+
+    if variant == "baseline":  # LayerNorm + GELU
+        cfg = H3BlockConfig(hidden=1536, heads=12, ffn=6144, precision=precision)
+    else:  # the reference model: RMSNorm, Q/K RMSNorm, SwiGLU
+        cfg = H3BlockConfig(hidden=1536, heads=12, ffn=4096, activation="swiglu", norm="rmsnorm",
+                            qk_norm=True, precision=precision)
+    s = 640
+    x, table, idx, cos, sin, w = _setup(cfg, s)
+    blk = H3DiTBlockB200(w, cfg, cuda_device)
+    dev = cuda_device
+    y = blk.forward(x.to(dev), table.to(dev), idx.to(dev), (cos.to(dev), sin.to(dev)))
+    torch.cuda.synchronize()
+    ref = ob.block_forward(x.float(), w, table, idx, cos, sin, cfg)
+    got = y.float().cpu()
+    assert torch.isfinite(got).all()
+    assert cosine((got - x.float()).numpy(), (ref - x.float()).numpy()) >= 0.99
+
+
+def test_norm_modulate_quant_matches_unfused(cuda_device):
+    """Fused prologue vs torch LayerNorm + the bit-exact indexed-affine kernel
+    + per-token quantisation."""
+    from xgen_b200.ops import indexed_affine, norm_modulate_quant, quantize_per_token
+
+    g = torch.Generator().manual_seed(4)
+    b, s, h = 2, 300, 3072
+    x = (3 * torch.randn(b, s, h, generator=g)).bfloat16().to(cuda_device)
+    table = torch.randn(5, 6 * h, generator=g).bfloat16().to(cuda_device)
+    shift, scale = table[:, :h], table[:, h:2 * h]
+    idx = torch.randint(5, (s,), generator=g).to(cuda_device)
+    codes, scales, mod = norm_modulate_quant(x, "layernorm", None, 1e-6, scale, shift, idx,
+                                             return_bf16=True)
+    n = torch.nn.functional.layer_norm(x.float(), (h,), eps=1e-6).bfloat16()
+    ref_mod = indexed_affine(n, scale, shift, idx, modulation=True)
+    d = (mod.float() - ref_mod.float()).abs()
+    # the fp32 LayerNorm statistics may round n differently by one bf16 ulp
+    assert (mod == ref_mod).float().mean() > 0.99
+    assert (d <= ref_mod.float().abs() * 2 ** -6 + 1e-6).all()
+    rc, rs = quantize_per_token(mod.reshape(b * s, h))
+    assert torch.equal(scales, rs) and torch.equal(codes.view(torch.uint8), rc.view(torch.uint8))

@@ -48,8 +48,10 @@ SIGNATURES = {
     "xgb_fp8_quantize_per_tensor": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "xgb_fp8_quantize_per_tensor_noalloc": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp]),
     "xgb_fp8_quantize_per_token": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]),
-    "xgb_fp8_gemm": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp,
-                             c_i64, c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp]),
+    "xgb_fp8_gemm": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_int,
+                             c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp]),
+    "xgb_norm_modulate_quant": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_float,
+                                        c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "xgb_sage_prepare_workspace": (c_i64, [c_i64, c_i64, c_i64]),
     "xgb_sage_prepare": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_int, c_i64, c_i64,
                                  c_i64, c_i64, c_float, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

@@ -40,7 +40,13 @@ constexpr int kBarOff = kStages * kStageBytes;
 constexpr int kSmem = kBarOff + 256 + 1024;
 constexpr uint32_t kIdesc = instr_desc(1, 0, 0, false, false, kBM, kBN);
 
-enum Epilogue : int { kPlain = 0, kGated = 1 };
+enum Epilogue : int { kPlain = 0, kGated = 1, kGeluErf = 2, kGeluTanh = 3 };
+
+// GELU of the FFN up projection: exact (erf) or the tanh approximation.
+__device__ __forceinline__ float gelu_erf(float y) { return 0.5f * y * (1.0f + erff(y * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu_tanh(float y) {
+  return 0.5f * y * (1.0f + tanhf(0.79788456080286536f * (y + 0.044715f * y * y * y)));
+}
 
 struct Params {
   int M, N, K;
@@ -190,6 +196,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float alpha = sa * p.sb[n * p.sb_stride];
               const float bias = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
               y[u] = fmaf(__uint_as_float(r[e + u]), alpha, bias);
+              if constexpr (kEpi == kGeluErf) y[u] = gelu_erf(y[u]);
+              if constexpr (kEpi == kGeluTanh) y[u] = gelu_tanh(y[u]);
               if constexpr (kEpi == kGated) {
                 // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
                 const float g = __bfloat162float(p.gate[grow * p.ldg + n]);
@@ -256,7 +264,8 @@ using namespace xgb;
 
 XGB_API int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t N, int64_t K,
                          const float* scale_a, int64_t scale_a_stride, const float* scale_w,
-                         int64_t scale_w_stride, const void* bias, void* out, int64_t ldo,
+                         int64_t scale_w_stride, const void* bias, int activation, void* out,
+                         int64_t ldo,
                          const void* gate, int64_t ldg, const int64_t* gate_index,
                          const void* residual, int64_t ldr, int* error_flag, void* stream) {
   if (!a || !w || !scale_a || !scale_w || !out) return XGB_ERR_ARG;
@@ -268,6 +277,7 @@ XGB_API int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t 
   if (ldo < N || ldo % 8) return XGB_ERR_STRIDE;
   const bool gated = gate != nullptr;
   if (gated && (!gate_index || !residual || ldr < N || ldg < N)) return XGB_ERR_ARG;
+  if (activation < 0 || activation > 2 || (gated && activation != 0)) return XGB_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) |
        reinterpret_cast<uintptr_t>(out)) & 15u)
     return XGB_ERR_ALIGN;
@@ -294,5 +304,8 @@ XGB_API int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t 
   p.ldr = ldr;
   p.err = error_flag;
   cudaStream_t st = as_stream(stream);
-  return gated ? gemm::launch<gemm::kGated>(a, w, p, st) : gemm::launch<gemm::kPlain>(a, w, p, st);
+  if (gated) return gemm::launch<gemm::kGated>(a, w, p, st);
+  if (activation == 1) return gemm::launch<gemm::kGeluErf>(a, w, p, st);
+  if (activation == 2) return gemm::launch<gemm::kGeluTanh>(a, w, p, st);
+  return gemm::launch<gemm::kPlain>(a, w, p, st);
 }

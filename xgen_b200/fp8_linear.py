@@ -100,6 +100,16 @@ class H3FP8Linear(nn.Module):
             raise ValueError("gated FP8 Linear needs bf16 gate rows [.., out] and a bf16 residual")
         return self._forward(x, (gate_table, gate_index, residual))
 
+    def forward_quantized(self, q, scale, activation: int = 0, gated=None, out_shape=None):
+        """GEMM on activations already quantised to e4m3 (q [M, in], scale
+        [M] per token or [1] per tensor), e.g. by the fused norm/modulate/
+        quant prologue. activation: 0 none, 1 GELU (erf), 2 GELU (tanh)."""
+        if q.dtype != torch.float8_e4m3fn or q.ndim != 2 or q.shape[1] != self.in_features:
+            raise ValueError("pre-quantised FP8 Linear input must be e4m3 [M, in]")
+        m = q.shape[0]
+        return self._gemm(q.contiguous(), scale.reshape(-1), 1 if scale.numel() > 1 else 0, m,
+                          q.device, activation, gated, out_shape or (m, self.out_features))
+
     def _forward(self, x, gated):
         self._check(x)
         matrix = x.reshape(-1, self.in_features)
@@ -108,7 +118,11 @@ class H3FP8Linear(nn.Module):
             return x.new_empty((*x.shape[:-1], self.out_features))
         matrix = matrix.contiguous()
         q, sa, sa_stride = self._quantize(matrix)
-        out = torch.empty((m, self.out_features), device=x.device, dtype=torch.bfloat16)
+        out = self._gemm(q, sa, sa_stride, m, x.device, 0, gated, (*x.shape[:-1], self.out_features))
+        return out if x.dtype == torch.bfloat16 else out.to(x.dtype)
+
+    def _gemm(self, q, sa, sa_stride, m, device, activation, gated, out_shape):
+        out = torch.empty((m, self.out_features), device=device, dtype=torch.bfloat16)
         gate = idx = res = None
         ldg = ldr = 0
         if gated is not None:
@@ -124,11 +138,10 @@ class H3FP8Linear(nn.Module):
         call("xgb_fp8_gemm", q.data_ptr(), self.weight.data_ptr(), m, self.out_features,
              self.in_features, sa.data_ptr(), sa_stride, self.weight_scale.data_ptr(),
              0 if self.weight_scale.numel() == 1 else 1,
-             self.bias.data_ptr() if self.bias is not None else None, out.data_ptr(),
+             self.bias.data_ptr() if self.bias is not None else None, activation, out.data_ptr(),
              self.out_features, gate.data_ptr() if gate is not None else None, ldg,
              idx.data_ptr() if idx is not None else None,
-             res.data_ptr() if res is not None else None, ldr, _err_flag(x.device).data_ptr(),
-             torch.cuda.current_stream(x.device).cuda_stream)
+             res.data_ptr() if res is not None else None, ldr, _err_flag(device).data_ptr(),
+             torch.cuda.current_stream(device).cuda_stream)
         self.calls += 1
-        out = out.reshape(*x.shape[:-1], self.out_features)
-        return out if x.dtype == torch.bfloat16 else out.to(x.dtype)
+        return out.reshape(out_shape)

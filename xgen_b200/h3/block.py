@@ -1,0 +1,139 @@
+"""The MiniMax-H3 DiT block on the B200 kernels.
+
+Block math as the reference composes it (h3_block_forward,
+x_diffusers/x_diffusers/framework/transformer/h3_npu_fusion.py:339-356, and
+fused_h3_block_forward, x_base/x_base/operator/h3_indexed_affine.py:52-61):
+
+    shift, scale, gate, shift_ff, scale_ff, gate_ff = adaln rows [idx]
+    n = norm1(x) * (1 + scale) + shift
+    x = x + gate * attn(n)            attn = to_out(SP attention(to_qkv(n)))
+    n = norm2(x) * (1 + scale_ff) + shift_ff
+    x = x + gate_ff * ff(n)           ff = down(act(up(n)))
+
+B200 mapping, per rank on its S_loc tokens:
+  norm + modulate + per-token e4m3       one fused kernel (xgb_norm_modulate_quant)
+  to_qkv                                 tcgen05 FP8 GEMM
+  Q/K RMSNorm (optional)                 xgb_qk_rms
+  RoPE + SP attention                    h3.sp_attention (PHAA FP8 wire at SP > 1)
+  to_out + gate + residual               FP8 GEMM with the gated epilogue
+  ff up + GELU                           FP8 GEMM with the GELU epilogue
+    (or up + gate-first SwiGLU kernel, the reference model's FFN)
+  ff down + gate_ff + residual           FP8 GEMM with the gated epilogue
+
+The AdaLN table is one [rows, 6*hidden] bf16 tensor in that order (the
+table-mode lookup of x_base/x_base/adaln_cache/cache.py:290-292).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ..attention import H3AttentionBackendB200
+from ..fp8_linear import H3FP8Linear
+from ..ops import gate_first_swiglu, norm_modulate_quant, quantize_per_token, try_h3_qk_rms
+from .sp_attention import sp_self_attention
+
+
+@dataclass
+class H3BlockConfig:
+    hidden: int = 3072
+    heads: int = 24
+    head_dim: int = 128
+    ffn: int = 12288
+    activation: str = "gelu"      # "gelu" or "swiglu" (reference model)
+    norm: str = "layernorm"       # "layernorm" (BASELINE) or "rmsnorm" (reference model)
+    qk_norm: bool = False         # per-head Q/K RMSNorm (reference model)
+    eps: float = 1e-6
+    precision: str = "sage"       # attention: "sage" or "bf16"
+    fp8_scaling: str = "per_token"
+
+
+class H3DiTBlockB200:
+    def __init__(self, weights: dict, config: H3BlockConfig, device):
+        c = self.config = config
+        self.device = device
+        lin = lambda name: H3FP8Linear(weights[name], weights.get(name + ".bias"),  # noqa: E731
+                                       scaling=c.fp8_scaling).to(device)
+        self.to_qkv = lin("to_qkv")
+        self.to_out = lin("to_out")
+        self.ff_up = lin("ff_up")
+        self.ff_down = lin("ff_down")
+        self.norm1_weight = weights.get("norm1.weight")
+        self.norm2_weight = weights.get("norm2.weight")
+        if self.norm1_weight is not None:
+            self.norm1_weight = self.norm1_weight.to(device, torch.bfloat16)
+            self.norm2_weight = weights["norm2.weight"].to(device, torch.bfloat16)
+        self.norm_q = self.norm_k = None
+        if c.qk_norm:
+            self.norm_q = torch.nn.RMSNorm(c.head_dim, eps=c.eps).to(device, torch.bfloat16)
+            self.norm_k = torch.nn.RMSNorm(c.head_dim, eps=c.eps).to(device, torch.bfloat16)
+            self.norm_q.weight.data.copy_(weights["norm_q.weight"])
+            self.norm_k.weight.data.copy_(weights["norm_k.weight"])
+        self.attention = H3AttentionBackendB200(c.precision)
+
+    @staticmethod
+    def random_weights(config: H3BlockConfig, seed: int = 0, std: float = 0.02) -> dict:
+        """Random-init weights of the block (N(0, std)), as BASELINE configs use."""
+        g = torch.Generator().manual_seed(seed)
+        h, f = config.hidden, config.ffn
+        up = 2 * f if config.activation == "swiglu" else f
+        w = {
+            "to_qkv": torch.randn(3 * h, h, generator=g) * std,
+            "to_out": torch.randn(h, h, generator=g) * std,
+            "ff_up": torch.randn(up, h, generator=g) * std,
+            "ff_down": torch.randn(h, f, generator=g) * std,
+        }
+        w = {k: v.bfloat16() for k, v in w.items()}
+        if config.norm == "rmsnorm":
+            w["norm1.weight"] = (1 + 0.1 * torch.randn(h, generator=g)).bfloat16()
+            w["norm2.weight"] = (1 + 0.1 * torch.randn(h, generator=g)).bfloat16()
+        if config.qk_norm:
+            w["norm_q.weight"] = (1 + 0.1 * torch.randn(config.head_dim, generator=g)).bfloat16()
+            w["norm_k.weight"] = (1 + 0.1 * torch.randn(config.head_dim, generator=g)).bfloat16()
+        return w
+
+    def forward(self, x, adaln_table, adaln_indices, rotary_emb, *, sp_group=None, sp_size=1,
+                phaa_num=2, fp8_transport=True, comm_stream=None, pad_key="mmh3_seq"):
+        """x [B, S_loc, hidden] bf16 -> [B, S_loc, hidden] bf16."""
+        c = self.config
+        b, s, h = x.shape
+        t = adaln_table
+        shift, scale, gate = t[:, 0:h], t[:, h:2 * h], t[:, 2 * h:3 * h]
+        shift_ff, scale_ff, gate_ff = t[:, 3 * h:4 * h], t[:, 4 * h:5 * h], t[:, 5 * h:6 * h]
+        idx = adaln_indices
+        with torch.no_grad():
+            # attention branch
+            a, sa = norm_modulate_quant(x, c.norm, self.norm1_weight, c.eps, scale, shift, idx)
+            qkv = self.to_qkv.forward_quantized(a, sa, out_shape=(b, s, 3 * h))
+            q, k, v = qkv[..., :h], qkv[..., h:2 * h], qkv[..., 2 * h:]
+            if c.qk_norm:
+                q4 = q.unflatten(-1, (c.heads, c.head_dim))
+                k4 = k.unflatten(-1, (c.heads, c.head_dim))
+                q4, k4 = try_h3_qk_rms(q4, k4, self.norm_q, self.norm_k)
+                q, k = q4.flatten(2), k4.flatten(2)
+            att = sp_self_attention(q, k, v, rotary_emb, backend=self.attention, heads=c.heads,
+                                    head_dim=c.head_dim, sp_group=sp_group, sp_size=sp_size,
+                                    phaa_num=phaa_num, fp8_transport=fp8_transport,
+                                    comm_stream=comm_stream, pad_key=pad_key)
+            x = self.to_out.forward_gated(att, gate, idx, x)
+            # feed-forward branch
+            a, sa = norm_modulate_quant(x, c.norm, self.norm2_weight, c.eps, scale_ff, shift_ff, idx)
+            if c.activation == "gelu":
+                hid = self.ff_up.forward_quantized(a, sa, activation=1)
+            else:
+                hid = gate_first_swiglu(self.ff_up.forward_quantized(a, sa))
+            hq, hs = quantize_per_token(hid)
+            m = b * s
+            res = x.reshape(m, h)
+            y = self.ff_down.forward_quantized(hq, hs, gated=(gate_ff, idx.repeat(b), res))
+            return y.reshape(b, s, h)
+
+    def flops(self, seq_local: int, seq_global: int) -> float:
+        """FLOPs of one block on one rank: the 4 GEMMs on its tokens plus its
+        share (heads / sp) of the attention over the full sequence."""
+        c = self.config
+        h, f = c.hidden, c.ffn
+        up = 2 * f if c.activation == "swiglu" else f
+        gemm = 2.0 * seq_local * (h * 3 * h + h * h + h * up + f * h)
+        return gemm

@@ -143,6 +143,31 @@ def quantize_activation(x: torch.Tensor):
     return out, scale
 
 
+def norm_modulate_quant(x: torch.Tensor, norm: str, weight, eps: float, scale: torch.Tensor,
+                        shift: torch.Tensor, indices: torch.Tensor, *, return_bf16: bool = False):
+    """Fused AdaLN prologue: per-token e4m3 of
+    bf16(bf16(norm(x) * bf16(1 + scale[idx])) + shift[idx]) for x [B, S, H]
+    (norm "layernorm" without affine or "rmsnorm" x weight); returns
+    (codes [B*S, H], scales [B*S]) and, with return_bf16, the modulated bf16."""
+    _require_cuda(x, scale, shift, indices, what="H3 norm/modulate")
+    if (x.ndim != 3 or x.dtype != torch.bfloat16 or x.stride(-1) != 1 or x.stride(0) != x.shape[1] * x.stride(1)
+            or scale.dtype != torch.bfloat16 or shift.dtype != torch.bfloat16
+            or scale.stride(-1) != 1 or shift.stride(-1) != 1 or indices.dtype != torch.int64
+            or indices.numel() != x.shape[1] or norm not in ("layernorm", "rmsnorm")):
+        raise ValueError("norm_modulate_quant needs bf16 [B,S,H] rows, bf16 tables, int64 [S] indices")
+    b, s, h = x.shape
+    rows = b * s
+    codes = torch.empty((rows, h), device=x.device, dtype=torch.float8_e4m3fn)
+    scales = torch.empty((rows,), device=x.device, dtype=torch.float32)
+    mod = torch.empty((b, s, h), device=x.device, dtype=torch.bfloat16) if return_bf16 else None
+    call("xgb_norm_modulate_quant", x.data_ptr(), x.stride(1), rows, h, s,
+         1 if norm == "rmsnorm" else 0, weight.data_ptr() if weight is not None else None,
+         float(eps), scale.data_ptr(), scale.stride(0), shift.data_ptr(), shift.stride(0),
+         indices.contiguous().data_ptr(), codes.data_ptr(), scales.data_ptr(),
+         mod.data_ptr() if mod is not None else None, _stream(x))
+    return (codes, scales, mod) if return_bf16 else (codes, scales)
+
+
 def quantize_per_token(x: torch.Tensor):
     """Per-row dynamic e4m3 of a 2-D bf16/fp16 matrix: (codes, scales[rows])."""
     _require_cuda(x, what="H3 FP8 quantization")
