@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--phaa-num", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-block", action="store_true", help="skip the full DiT block timing")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the attention kernel on --seq/--heads (profiling case)")
@@ -366,6 +367,11 @@ def main():
                "sample": f"fp32 SDPA (oracle port of attention.py:29-34) on 1 head: "
                          f"{flops / 4 / SEQ / HEAD_DIM:.0f} query rows x {SEQ} keys in {secs:.1f}s"}
 
+    block = None
+    if not args.no_block:
+        block = block_timing(args, world, rank, dev, group, s_loc, cos, sin, comm_stream, barrier,
+                             max_over_ranks)
+
     kernels_per_layer = kernels_per_step(args.precision, world, min(args.phaa_num, HEADS // world))
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
@@ -376,12 +382,63 @@ def main():
         "per_gpu_tflops": value / world, "attention_calls_per_step": attn_calls,
         "gpu_launches": kernels_per_layer * args.steps,
         "clocks": clocks.summary(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+        "block": block,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     del out
     if world > 1:
         dist.destroy_process_group()
+
+
+def block_timing(args, world, rank, dev, group, s_loc, cos, sin, comm_stream, barrier,
+                 max_over_ranks):
+    """The metric's "DiT block ms": one full H3 DiT block (BASELINE config 4/5
+    dimensions: hidden 3072, 24 x 128 heads, GELU FFN 12288, AdaLN LayerNorm
+    from a cached random 6 x 3072 table per modality) at 768P-5s on this
+    rank's S_loc tokens: fused norm/modulate/quant, FP8 QKV, SP attention
+    (PHAA FP8 wire at N > 1), FP8 to_out + gated residual, FP8 FFN with the
+    GELU epilogue and gated residual. Random-init weights N(0, 0.02)."""
+    import torch
+
+    from xgen_b200.h3.block import H3BlockConfig, H3DiTBlockB200
+
+    cfg = H3BlockConfig(hidden=3072, heads=HEADS, head_dim=HEAD_DIM, ffn=12288,
+                        activation="gelu", norm="layernorm", precision=args.precision)
+    blk = H3DiTBlockB200(H3DiTBlockB200.random_weights(cfg, seed=0), cfg, dev)
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    x = torch.randn(1, s_loc, cfg.hidden, device=dev, generator=g).bfloat16()
+    table = (0.1 * torch.randn(3, 6 * cfg.hidden, device=dev,
+                               generator=torch.Generator(device=dev).manual_seed(5))).bfloat16()
+    # modality tag per token (video 0, text 1, audio 2) of this rank's span
+    tags = torch.zeros(SEQ + world * 16, dtype=torch.int64)
+    video = GRID[0] * GRID[1] * GRID[2]
+    tags[video:video + TEXT] = 1
+    tags[video + TEXT:SEQ] = 2
+    idx = tags[rank * s_loc:(rank + 1) * s_loc].to(dev)
+
+    def run():
+        return blk.forward(x, table, idx, (cos, sin), sp_group=group, sp_size=world,
+                           phaa_num=min(args.phaa_num, HEADS // world),
+                           fp8_transport=args.precision == "sage", comm_stream=comm_stream)
+
+    for _ in range(max(3, args.warmup)):
+        run()
+    barrier()
+    steps = max(2, min(args.steps, 5))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        run()
+    e.record()
+    barrier()
+    ms = max_over_ranks(s.elapsed_time(e) / steps)
+    gemm_flops = blk.flops(s_loc, SEQ) * world
+    total = gemm_flops + FLOPS_PER_LAYER
+    return {"ms": ms, "steps": steps, "tflops_aggregate": total / ms / 1e9,
+            "tflops_per_gpu": total / ms / 1e9 / world, "gemm_flops": gemm_flops,
+            "attention_flops": FLOPS_PER_LAYER,
+            "config": "hidden 3072, 24x128 heads, FFN 12288 GELU, AdaLN LayerNorm, FP8 per-token linears"}
 
 
 def kernels_per_step(precision, world, phaa):
