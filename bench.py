@@ -531,31 +531,54 @@ def profile_traffic(precision, heads):
 
 
 def end_to_end(step, q, k, v, args, world, dev, barrier, max_over_ranks):
-    """Same layer through the public API with pinned host buffers: H2D of
-    the step's Q/K/V shard and D2H of its output inside the timed region."""
+    """Same layer through the public API with pinned host buffers: every
+    step's Q/K/V shard is copied host->device and its output device->host
+    inside the timed region. The copies run on a side stream with two device
+    buffer sets, so step i+1's upload and step i-1's download overlap step
+    i's compute (the way a serving loop would feed the layer)."""
     import torch
 
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    houts = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2)]
     steps = max(2, min(args.steps, 5))
-    dq, dk, dv = (torch.empty_like(t) for t in (q, k, v))
+    bufs = [tuple(torch.empty_like(t) for t in (q, k, v)) for _ in range(2)]
+    cs = torch.cuda.current_stream(dev)
+    xs = torch.cuda.Stream(device=dev)
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
 
-    def one():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        out = step(dq, dk, dv)
-        hout.copy_(out, non_blocking=True)
+    def upload(i):
+        with torch.cuda.stream(xs):
+            if i >= 2:
+                xs.wait_event(computed[i % 2])  # step i-2 has finished reading this set
+            for d, h in zip(bufs[i % 2], (hq, hk, hv)):
+                d.copy_(h, non_blocking=True)
+            loaded[i % 2].record(xs)
 
-    one()
+    def run(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            cs.wait_event(loaded[i % 2])
+            out = step(*bufs[i % 2])
+            computed[i % 2].record(cs)
+            with torch.cuda.stream(xs):
+                xs.wait_event(computed[i % 2])
+                houts[i % 2].copy_(out, non_blocking=True)
+                out.record_stream(xs)
+        cs.wait_stream(xs)
+
+    run(2)
     barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        one()
-    e.record()
+    s.record(cs)
+    xs.wait_event(s)
+    run(steps)
+    e.record(cs)
     barrier()
     ms = max_over_ranks(s.elapsed_time(e) / steps)
+    hout = houts[0]
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
     return {"value": FLOPS_PER_LAYER / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,

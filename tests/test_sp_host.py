@@ -108,9 +108,11 @@ def _worker(rank, world, port, q, k, v, heads, d, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("s", [24, 23])
-def test_two_rank_sp_matches_single_rank(s):
-    heads, d = 4, 32
+@pytest.mark.parametrize("s,heads", [(24, 4), (23, 4), (21, 6)])
+def test_two_rank_sp_matches_single_rank(s, heads):
+    # heads=6 on 2 ranks gives 3 local heads in PHAA chunks [2, 1], the
+    # uneven split of 24 heads at SP8
+    d = 32
     g = torch.Generator().manual_seed(s)
     q, k, v = (torch.randn(1, s, heads * d, generator=g).bfloat16() for _ in range(3))
     expect = _sdpa(*(t.unflatten(-1, (heads, d)).transpose(1, 2) for t in (q, k, v)))
