@@ -112,6 +112,35 @@ int xgb_fp8_wire_decode(const uint8_t* payload, void* const* dests, int streams,
                         int64_t peers, int64_t width, int64_t peer_padding, int dtype,
                         void* stream);
 
+/* xgb_fp8_wire_encode with a sequence mask: rows whose global sequence
+ * index peer*seq + s is >= valid_seq are not read and encode as zeros with
+ * scale 1e-12 (0 < valid_seq <= peers*seq; peers*seq means all rows). The
+ * async exchange's fused return pack encodes the attention output
+ * [batch, head, valid_seq, D] through the view [peers, seq, batch, head]
+ * with strides (seq*sS, sS, sB, sH).
+ * Replaces _encode with RETURN_SEQ / STRIDED,
+ * x_base/x_base/phaa/fp8_async_transport.py:14-50, and _pack_exchange,
+ * :129-181. */
+int xgb_fp8_wire_encode_view(const void* const* sources, const int64_t* strides, int streams,
+                             int64_t peers, int64_t seq, int64_t batch, int64_t heads,
+                             int64_t width, int dtype, const float* cos, const float* sin,
+                             int64_t rotary, int64_t valid_seq, int64_t peer_padding,
+                             uint8_t* payload, void* stream);
+
+/* Decode the wire into `streams` destinations addressed, like the encode's
+ * sources, as [peers, seq, batch, heads] views with element strides
+ * strides[4*s + 0..3] (channel stride 1); rows with peer*seq + s >=
+ * valid_seq are skipped. Wire rows are in [peer, seq, batch, head] order.
+ * Covers the direct gather (destination = attention input [batch, head,
+ * valid_seq, D]) and the direct return (destination = [batch, seq, heads*D]
+ * at the chunk's head offset) of the async exchange.
+ * Replaces _decode / _unpack_exchange,
+ * x_base/x_base/phaa/fp8_async_transport.py:53-81, :184-193. */
+int xgb_fp8_wire_decode_view(const uint8_t* payload, void* const* dests, const int64_t* strides,
+                             int streams, int64_t peers, int64_t seq, int64_t batch,
+                             int64_t heads, int64_t width, int64_t valid_seq,
+                             int64_t peer_padding, int dtype, void* stream);
+
 /* ---- FP8 Linear activation quantisation ---- */
 
 /* Bytes of workspace xgb_fp8_quantize_per_tensor needs for n elements. */

@@ -77,6 +77,15 @@ def test_phaa_option_validation():
         phaa.run_phaa_attention(q, q, q, tail_first=True, **common)
     with pytest.raises(ValueError, match="FP8 transport requires CUDA"):
         phaa.run_phaa_attention(q, q, q, fp8_transport=True, **common)
+    from xgen_b200.phaa.fp8_async_transport import AsyncFP8Options
+    with pytest.raises(ValueError, match="fused return pack requires direct return"):
+        AsyncFP8Options(fused_return_pack=True)
+    with pytest.raises(ValueError, match="async exchange requires device join"):
+        phaa.run_phaa_attention(q, q, q, fp8_transport=True, async_options=AsyncFP8Options(),
+                                **common)
+    with pytest.raises(ValueError, match="device join requires single-stream FP8"):
+        phaa.run_phaa_attention(q, q, q, device_join=True, async_options=AsyncFP8Options(),
+                                **common)
 
 
 # ------------------------------------------------------------------ 2 gloo ranks

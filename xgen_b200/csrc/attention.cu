@@ -66,6 +66,19 @@ constexpr int kPolyEvery = XGB_ATTN_POLY_EVERY;
 __device__ __forceinline__ bool use_poly(int idx) {
   return kPolyEvery > 0 && idx % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1;
 }
+// With kPolyPairs > 0, one pair of exp2 in kPolyPairs runs as a packed
+// fp32x2 polynomial (ex2_poly2) instead of two MUFU ops.
+#ifndef XGB_ATTN_POLY_PAIRS
+#define XGB_ATTN_POLY_PAIRS 0
+#endif
+constexpr int kPolyPairs = XGB_ATTN_POLY_PAIRS;
+__device__ __forceinline__ bool poly_pair(int pair) {
+  return kPolyPairs > 0 && pair % (kPolyPairs > 0 ? kPolyPairs : 1) == kPolyPairs - 1;
+}
+#ifndef XGB_ATTN_TURN
+#define XGB_ATTN_TURN 1
+#endif
+constexpr bool kTurn = XGB_ATTN_TURN != 0;
 
 template <bool kSage>
 struct Cfg {
@@ -299,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The two warpgroups take turns in the MUFU-bound exp section so one's
     // exp overlaps the other's load/max/rescale work; WG1 hands the first
     // turn to WG0.
-    if (i == 1) mbar_arrive(&bars->turn[0]);
+    if (kTurn && i == 1) mbar_arrive(&bars->turn[0]);
     for (int t = 0; t < n_kv; ++t) {
       const uint32_t s_addr = lane_addr + s_col(i, t & 1);
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[i][t & 1], (t >> 1) & 1, p.err));
@@ -369,8 +382,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(&bars->turn[i], t & 1, p.err));
-      if (!ok) break;
+      if constexpr (kTurn) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->turn[i], t & 1, p.err));
+        if (!ok) break;
+      }
       // P = exp2(comb*s - m_used) (times kPScale for e4m3, folded into the
       // exponent), row sum, pack and store over the S buffer.
       // Row sums in four independent packed chains (short dependency chains).
@@ -386,8 +401,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             ffma2(x[0], x[1], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb, off, off);
             ffma2(x[2], x[3], __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]), comb, comb, off, off);
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              pv[u] = use_poly(e + u) ? ex2_poly(x[u]) : ex2_approx(x[u]);
+            for (int u = 0; u < 4; u += 2) {
+              if (poly_pair((c * 32 + e + u) / 2)) {
+                ex2_poly2<2>(pv[u], pv[u + 1], x[u], x[u + 1]);
+              } else {
+                pv[u] = use_poly(e + u) ? ex2_poly(x[u]) : ex2_approx(x[u]);
+                pv[u + 1] = use_poly(e + u + 1) ? ex2_poly(x[u + 1]) : ex2_approx(x[u + 1]);
+              }
+            }
             const int ch = (e / 4) & 1;
             fadd2(rsa[2 * ch], rsb[2 * ch], rsa[2 * ch], rsb[2 * ch], pv[0], pv[1]);
             fadd2(rsa[2 * ch + 1], rsb[2 * ch + 1], rsa[2 * ch + 1], rsb[2 * ch + 1], pv[2], pv[3]);
@@ -404,8 +425,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; e += 2) {
             float xa, xb;
             ffma2(xa, xb, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb, off, off);
-            const float a = ex2_approx(xa);
-            const float b = use_poly(e + 1) ? ex2_poly(xb) : ex2_approx(xb);
+            float a, b;
+            if (poly_pair((c * 32 + e) / 2)) {
+              ex2_poly2<3>(a, b, xa, xb);
+            } else {
+              a = ex2_approx(xa);
+              b = use_poly(e + 1) ? ex2_poly(xb) : ex2_approx(xb);
+            }
             const int ch = (e / 2) & 3;
             fadd2(rsa[ch], rsb[ch], rsa[ch], rsb[ch], a, b);
             packed[e / 2] = pack_bf16x2(a, b);
@@ -413,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(s_addr + c * 16, packed);
         }
       }
-      mbar_arrive(&bars->turn[i ^ 1]);
+      if constexpr (kTurn) mbar_arrive(&bars->turn[i ^ 1]);
       l += ((rsa[0] + rsb[0]) + (rsa[1] + rsb[1])) + ((rsa[2] + rsb[2]) + (rsa[3] + rsb[3]));
       tmem_st_wait();
       tc_fence_before();

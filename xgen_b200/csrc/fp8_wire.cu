@@ -8,6 +8,15 @@
 // The division is IEEE (__fdiv_rn), matching the reference algorithm as the
 // Triton interpreter evaluates it.
 //
+// Rows are addressed through [peer, seq, batch, head] views with any element
+// strides (unit channel stride) on both sides, so the async exchange's
+// direct layouts (x_base/x_base/phaa/fp8_async_transport.py:14-81) need no
+// copies: the return pack reads the attention output [batch, head, seq, D]
+// and the direct gather / direct return decodes write the attention input
+// [batch, head, seq, D] and the final [batch, seq, heads*D] in place. A row
+// whose global sequence index peer*seq + s is >= valid_seq encodes as zeros
+// (scale 1e-12) without a load and is skipped by the decode.
+//
 // Work split: a group of G = next_pow2(width/8) lanes owns one row, each lane
 // 8 channels; 32/G rows per warp, so width=128 uses full warps (2 rows each).
 #include "xgb_common.cuh"
@@ -21,7 +30,7 @@ constexpr int kMaxStreams = 3;
 struct EncodeArgs {
   const void* src[kMaxStreams];
   int64_t st[kMaxStreams][4];  // element strides: peer, seq, batch, head
-  int64_t peers, seq, batch, heads, width, rows, peer_rows, peer_padding;
+  int64_t peers, seq, batch, heads, width, rows, peer_rows, peer_padding, valid_seq;
   int streams;
   const float* cos;
   const float* sin;
@@ -70,14 +79,16 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
   const int64_t bat = (r / a.heads) % a.batch;
   const int64_t s = (r / (a.heads * a.batch)) % a.seq;
   const int64_t peer = r / a.peer_rows;
-  const T* src = static_cast<const T*>(a.src[slot]) + peer * a.st[slot][0] + s * a.st[slot][1] +
-                 bat * a.st[slot][2] + head * a.st[slot][3];
+  const bool inside = peer * a.seq + s < a.valid_seq;
+  const T* src = static_cast<const T*>(a.src[slot]);
+  if (inside) src += peer * a.st[slot][0] + s * a.st[slot][1] + bat * a.st[slot][2] + head * a.st[slot][3];
   const int c0 = sub * 8;
   const int valid = live ? max(0, min(8, static_cast<int>(a.width) - c0)) : 0;
+  const int loaded = inside ? valid : 0;
 
   float x[8];
-  load_row8<T, kVec>(src + c0, valid, x);
-  if (a.rotary > 0 && slot < 2 && c0 < a.rotary) {
+  load_row8<T, kVec>(src + c0, loaded, x);
+  if (inside && a.rotary > 0 && slot < 2 && c0 < a.rotary) {
     // Fused pre-A2A RoPE (h3_partial_rope.py:9-29): bf16 result, then encode.
     const int64_t half = a.rotary / 2;
     float p[8];
@@ -129,7 +140,8 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
 struct DecodeArgs {
   const uint8_t* payload;
   void* dst[kMaxStreams];
-  int64_t width, rows, peer_rows, peer_padding;
+  int64_t st[kMaxStreams][4];  // element strides of the destination: peer, seq, batch, head
+  int64_t seq, batch, heads, width, rows, peer_rows, peer_padding, valid_seq;
   int streams;
 };
 
@@ -146,10 +158,15 @@ __global__ void __launch_bounds__(kThreads) wire_decode_kernel(DecodeArgs a, int
   const int valid = max(0, min(8, static_cast<int>(a.width) - c0));
   if (valid == 0) return;
   const int64_t peer = row / a.peer_rows;
+  const int64_t head = row % a.heads;
+  const int64_t bat = (row / a.heads) % a.batch;
+  const int64_t s = (row / (a.heads * a.batch)) % a.seq;
+  if (peer * a.seq + s >= a.valid_seq) return;
   const int64_t wire_row = row + (peer * (a.streams - 1) + slot) * a.peer_rows;
   const uint8_t* src = a.payload + wire_row * (a.width + 4) + peer * a.peer_padding;
   const float scale = __ldg(reinterpret_cast<const float*>(src + a.width));
-  T* dst = static_cast<T*>(a.dst[slot]) + row * a.width + c0;
+  T* dst = static_cast<T*>(a.dst[slot]) + peer * a.st[slot][0] + s * a.st[slot][1] +
+           bat * a.st[slot][2] + head * a.st[slot][3] + c0;
   uint8_t b[8];
   if (valid == 8) {
     *reinterpret_cast<uint32_t*>(b) = __ldg(reinterpret_cast<const uint32_t*>(src + c0));
@@ -179,15 +196,16 @@ int group_for(int64_t width) {
 
 using namespace xgb;
 
-XGB_API int xgb_fp8_wire_encode(const void* const* sources, const int64_t* strides, int streams,
-                                int64_t peers, int64_t seq, int64_t batch, int64_t heads,
-                                int64_t width, int dtype, const float* cos, const float* sin,
-                                int64_t rotary, int64_t peer_padding, uint8_t* payload,
-                                void* stream) {
+XGB_API int xgb_fp8_wire_encode_view(const void* const* sources, const int64_t* strides,
+                                     int streams, int64_t peers, int64_t seq, int64_t batch,
+                                     int64_t heads, int64_t width, int dtype, const float* cos,
+                                     const float* sin, int64_t rotary, int64_t valid_seq,
+                                     int64_t peer_padding, uint8_t* payload, void* stream) {
   if (!sources || !strides || !payload) return XGB_ERR_ARG;
   if (streams != 1 && streams != 3) return XGB_ERR_ARG;
   if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
   if (peers <= 0 || seq < 0 || batch < 0 || heads < 0) return XGB_ERR_SHAPE;
+  if (valid_seq < 0 || valid_seq > peers * seq) return XGB_ERR_SHAPE;
   if (width <= 0 || width % 4 || width > 256) return XGB_ERR_SHAPE;
   if (peer_padding < 0 || peer_padding >= 16 || peer_padding % 4) return XGB_ERR_ARG;
   if (rotary < 0 || rotary % 2 || rotary > width) return XGB_ERR_SHAPE;
@@ -208,7 +226,7 @@ XGB_API int xgb_fp8_wire_encode(const void* const* sources, const int64_t* strid
   if (width % 8) vec = false;
   a.peers = peers; a.seq = seq; a.batch = batch; a.heads = heads; a.width = width;
   a.peer_rows = a.rows / peers;
-  a.peer_padding = peer_padding; a.streams = streams;
+  a.peer_padding = peer_padding; a.streams = streams; a.valid_seq = valid_seq;
   a.cos = cos; a.sin = sin; a.rotary = rotary; a.payload = payload;
   const int group = group_for(width);
   const int64_t rows_per_block = (kThreads / 32) * (32 / group);
@@ -224,29 +242,64 @@ XGB_API int xgb_fp8_wire_encode(const void* const* sources, const int64_t* strid
   return launch_status();
 }
 
-XGB_API int xgb_fp8_wire_decode(const uint8_t* payload, void* const* dests, int streams,
-                                int64_t rows, int64_t peers, int64_t width, int64_t peer_padding,
-                                int dtype, void* stream) {
-  if (!payload || !dests) return XGB_ERR_ARG;
+XGB_API int xgb_fp8_wire_encode(const void* const* sources, const int64_t* strides, int streams,
+                                int64_t peers, int64_t seq, int64_t batch, int64_t heads,
+                                int64_t width, int dtype, const float* cos, const float* sin,
+                                int64_t rotary, int64_t peer_padding, uint8_t* payload,
+                                void* stream) {
+  if (peers <= 0 || seq < 0) return XGB_ERR_SHAPE;
+  return xgb_fp8_wire_encode_view(sources, strides, streams, peers, seq, batch, heads, width,
+                                  dtype, cos, sin, rotary, peers * seq, peer_padding, payload,
+                                  stream);
+}
+
+XGB_API int xgb_fp8_wire_decode_view(const uint8_t* payload, void* const* dests,
+                                     const int64_t* strides, int streams, int64_t peers,
+                                     int64_t seq, int64_t batch, int64_t heads, int64_t width,
+                                     int64_t valid_seq, int64_t peer_padding, int dtype,
+                                     void* stream) {
+  if (!payload || !dests || !strides) return XGB_ERR_ARG;
   if (streams != 1 && streams != 3) return XGB_ERR_ARG;
   if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
-  if (rows < 0 || peers <= 0 || rows % peers) return XGB_ERR_SHAPE;
+  if (peers <= 0 || seq < 0 || batch < 0 || heads < 0) return XGB_ERR_SHAPE;
+  if (valid_seq < 0 || valid_seq > peers * seq) return XGB_ERR_SHAPE;
   if (width <= 0 || width % 4 || width > 256) return XGB_ERR_SHAPE;
   if (peer_padding < 0 || peer_padding >= 16 || peer_padding % 4) return XGB_ERR_ARG;
-  if (rows == 0) return XGB_OK;
   DecodeArgs a{};
+  a.rows = peers * seq * batch * heads;
+  if (a.rows == 0) return XGB_OK;
   a.payload = payload;
   for (int s = 0; s < streams; ++s) {
     if (!dests[s]) return XGB_ERR_ARG;
     a.dst[s] = dests[s];
+    for (int d = 0; d < 4; ++d) a.st[s][d] = strides[4 * s + d];
   }
-  a.width = width; a.rows = rows; a.peer_rows = rows / peers;
-  a.peer_padding = peer_padding; a.streams = streams;
+  a.seq = seq; a.batch = batch; a.heads = heads; a.width = width;
+  a.peer_rows = a.rows / peers;
+  a.peer_padding = peer_padding; a.streams = streams; a.valid_seq = valid_seq;
   const int group = group_for(width);
   const int64_t rows_per_block = (kThreads / 32) * (32 / group);
-  dim3 grid(static_cast<unsigned>(cdiv(rows, rows_per_block)), streams);
+  dim3 grid(static_cast<unsigned>(cdiv(a.rows, rows_per_block)), streams);
   cudaStream_t st = as_stream(stream);
   if (dtype == XGB_BF16) wire_decode_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(a, group);
   else wire_decode_kernel<__half><<<grid, kThreads, 0, st>>>(a, group);
   return launch_status();
+}
+
+XGB_API int xgb_fp8_wire_decode(const uint8_t* payload, void* const* dests, int streams,
+                                int64_t rows, int64_t peers, int64_t width, int64_t peer_padding,
+                                int dtype, void* stream) {
+  if (rows < 0 || peers <= 0 || rows % peers) return XGB_ERR_SHAPE;
+  if (width <= 0) return XGB_ERR_SHAPE;
+  const int64_t peer_rows = rows / peers;
+  // Contiguous destinations: [peer, row, 1, 1] with row stride `width`.
+  int64_t strides[4 * kMaxStreams];
+  for (int s = 0; s < kMaxStreams; ++s) {
+    strides[4 * s + 0] = peer_rows * width;
+    strides[4 * s + 1] = width;
+    strides[4 * s + 2] = 0;
+    strides[4 * s + 3] = 0;
+  }
+  return xgb_fp8_wire_decode_view(payload, dests, strides, streams, peers, peer_rows, 1, 1, width,
+                                  rows, peer_padding, dtype, stream);
 }

@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import logging
 import os
+from typing import NamedTuple
 
 import torch
 import torch.distributed as dist
@@ -36,6 +37,24 @@ def peer_alignment_metrics():
     return dict(_peer_alignment_metrics)
 
 
+class WireView(NamedTuple):
+    """Rows of `head_dim` channels of one tensor addressed as
+    [peer, seq, batch, head] with element strides (unit channel stride).
+    Unlike a torch view it may describe rows beyond the tensor (global
+    sequence index >= valid_seq), which the codec never touches."""
+    ptr: int
+    shape: tuple
+    strides: tuple
+    dtype: torch.dtype
+
+    @staticmethod
+    def of(t: torch.Tensor) -> "WireView":
+        """From a 5-D [peer, seq, batch, head, head_dim] tensor view."""
+        if t.ndim != 5 or t.stride(-1) != 1:
+            raise ValueError("PHAA FP8 wire views are 5-D with unit channel stride")
+        return WireView(t.data_ptr(), tuple(t.shape[:4]), tuple(t.stride()[:4]), t.dtype)
+
+
 def _rows_view(t: torch.Tensor, peers: int, head_dim: int) -> torch.Tensor:
     """A [peer, seq, batch, head, head_dim] view of `t` whose lexicographic
     row order equals the reference's flattened row order."""
@@ -51,29 +70,36 @@ def _rows_view(t: torch.Tensor, peers: int, head_dim: int) -> torch.Tensor:
 
 
 def encode(tensors, head_dim: int, peers: int, *, peer_padding: int = 0, rotary_emb=None,
-           out: torch.Tensor | None = None) -> torch.Tensor:
-    """Encode 1 or 3 tensors into the PHAA byte wire (a flat uint8 tensor)."""
+           out: torch.Tensor | None = None, views=None, valid_seq: int | None = None
+           ) -> torch.Tensor:
+    """Encode 1 or 3 tensors into the PHAA byte wire (a flat uint8 tensor).
+
+    `views`, when given, are `WireView`s of the sources (any strides, unit
+    channel stride); rows whose global sequence index peer*seq + s reaches
+    `valid_seq` encode as zeros without being read."""
     streams = len(tensors)
-    views = [_rows_view(t, peers, head_dim) for t in tensors]
+    if views is None:
+        # `rows` keeps any contiguous copies alive until the kernel is queued.
+        rows = [_rows_view(t, peers, head_dim) for t in tensors]
+        views = [WireView.of(r) for r in rows]
     shape = views[0].shape
     if any(v.shape != shape for v in views):
         raise ValueError("PHAA FP8 transport requires matching shapes")
-    rows = views[0].numel() // head_dim
-    peer_rows = rows // peers
+    peer_rows = shape[1] * shape[2] * shape[3]
     nbytes = peers * (peer_rows * streams * (head_dim + 4) + peer_padding)
     wire = out if out is not None else torch.empty(nbytes, dtype=torch.uint8,
                                                     device=tensors[0].device)
-    strides = [s for v in views for s in v.stride()[:4]]
+    strides = [s for v in views for s in v.strides]
     cos = sin = None
     rotary = 0
     if rotary_emb is not None:
         cos, sin = rotary_emb
         rotary = cos.shape[-1]
-    call("xgb_fp8_wire_encode", ptr_array(v.data_ptr() for v in views), i64_array(strides),
+    call("xgb_fp8_wire_encode_view", ptr_array(v.ptr for v in views), i64_array(strides),
          streams, shape[0], shape[1], shape[2], shape[3], head_dim, _DTYPE[tensors[0].dtype],
          cos.data_ptr() if cos is not None else None, sin.data_ptr() if sin is not None else None,
-         rotary, peer_padding, wire.data_ptr(),
-         torch.cuda.current_stream(tensors[0].device).cuda_stream)
+         rotary, shape[0] * shape[1] if valid_seq is None else valid_seq, peer_padding,
+         wire.data_ptr(), torch.cuda.current_stream(tensors[0].device).cuda_stream)
     return wire
 
 
@@ -84,6 +110,20 @@ def decode(wire: torch.Tensor, outputs, head_dim: int, peers: int, *, peer_paddi
     call("xgb_fp8_wire_decode", wire.data_ptr(), ptr_array(o.data_ptr() for o in outputs),
          streams, rows, peers, head_dim, peer_padding, _DTYPE[outputs[0].dtype],
          torch.cuda.current_stream(wire.device).cuda_stream)
+
+
+def decode_view(wire: torch.Tensor, views, head_dim: int, *, valid_seq: int | None = None,
+                peer_padding: int = 0):
+    """Decode the wire into `WireView` destinations, skipping rows whose
+    global sequence index peer*seq + s reaches `valid_seq`."""
+    shape = views[0].shape
+    if any(v.shape != shape for v in views):
+        raise ValueError("PHAA FP8 decode views must match")
+    strides = [s for v in views for s in v.strides]
+    call("xgb_fp8_wire_decode_view", wire.data_ptr(), ptr_array(v.ptr for v in views),
+         i64_array(strides), len(views), shape[0], shape[1], shape[2], shape[3], head_dim,
+         shape[0] * shape[1] if valid_seq is None else valid_seq, peer_padding,
+         _DTYPE[views[0].dtype], torch.cuda.current_stream(wire.device).cuda_stream)
 
 
 def fp8_all_to_all(output, tensor, head_dim, group):

@@ -8,6 +8,12 @@ device or host join. The local heads are split into `phaa_split_num` chunks
 `comm_stream` while chunk i's attention runs on the compute stream, and each
 chunk's output returns by its own A2A.
 
+With `async_options` (an `AsyncFP8Options`; requires FP8 transport and
+device join) every exchange is an async NCCL collective submitted on
+`comm_stream` and joined on the consuming stream (`submit_fp8_exchange` /
+`finish_fp8_exchange`), optionally with the direct gather, fused return pack
+and direct return layouts (phaa_attention.py:84-107, :150-327).
+
 B200 extension: `fuse_rope=True` with `rotary_emb=(cos, sin)` applies the
 partial RoPE to Q and K inside the FP8 wire encode (the reference applies it
 in a separate pass before PHAA; the bytes on the wire are identical).
@@ -62,7 +68,7 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
                        attention_mask=None, pad_key="pad", attention_fn=None,
                        fp8_transport=False, gather_priority=False, scatter_stream=None,
                        scatter_group=None, tail_first=False, device_join=False,
-                       fuse_rope=False):
+                       async_options=None, fuse_rope=False):
     """query/key/value (B, S_loc, heads*head_dim) -> (B, S_loc, heads*head_dim)."""
     W_S = sp_size
     B, Sq, H = query.shape
@@ -75,6 +81,12 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
         raise ValueError("PHAA gather priority requires FP8 transport")
     if device_join and (not fp8_transport or scatter_stream is not None):
         raise ValueError("PHAA device join requires single-stream FP8 transport")
+    async_exchange = async_options is not None
+    direct_gather = async_exchange and async_options.direct_gather
+    direct_return = async_exchange and async_options.direct_return
+    fused_return_pack = async_exchange and async_options.fused_return_pack
+    if async_exchange and not device_join:
+        raise ValueError("PHAA async exchange requires device join")
     if (scatter_stream is None) != (scatter_group is None) or (
             scatter_stream is not None and not fp8_transport):
         raise ValueError("Separate PHAA scatter requires FP8, a stream and a process group")
@@ -107,15 +119,34 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
     for c in range(phaa_split_num):
         o, cs = offsets[c], sizes[c]
         chunks.append(tuple(t[:, :, :, o:o + cs, :].permute(2, 1, 0, 3, 4) for t in (q5, k5, v5)))
-    gather = [tuple(torch.empty((W_S, Sq, B, cs, D), device=query.device, dtype=query.dtype)
+    def gather_shape(cs):
+        if direct_gather:
+            return (B, cs, W_S * Sq - pad, D)
+        return (W_S, Sq, B, cs, D)
+
+    gather = [tuple(torch.empty(gather_shape(cs), device=query.device, dtype=query.dtype)
                     for _ in range(3)) for cs in sizes]
-    returned = [torch.empty((W_S, Sq, B, cs * D), device=query.device, dtype=query.dtype)
-                for cs in sizes]
+    if direct_return:
+        final = torch.empty((B, Sq, H), device=query.device, dtype=query.dtype)
+        returned = None
+    else:
+        returned = [torch.empty((W_S, Sq, B, cs * D), device=query.device, dtype=query.dtype)
+                    for cs in sizes]
+    pending_gathers, pending_returns = {}, []
+    if async_exchange:
+        from .fp8_async_transport import finish_fp8_exchange, submit_fp8_exchange
     gathered = [acc.Event() for _ in sizes]
     attended = [acc.Event() for _ in sizes]
     results = [None] * phaa_split_num
 
     def gather_chunk(i):
+        if async_exchange:
+            pending_gathers[i] = submit_fp8_exchange(
+                gather[i], chunks[i], D, sp_group, row_tiling=async_options.row_tiling,
+                direct_gather=direct_gather, rotary_emb=rotary_emb if fuse_rope else None)
+            for t in chunks[i]:
+                t.record_stream(comm_stream)
+            return
         if fp8_transport:
             fp8.fp8_all_to_all_many(gather[i], chunks[i], D, sp_group,
                                     rotary_emb=rotary_emb if fuse_rope else None)
@@ -132,14 +163,24 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             gather_chunk(i)
 
     for pos, step in enumerate(order):
-        acc.current_stream().wait_event(gathered[step])
-        qv, kv, vv = (x.flatten(0, 1).permute(1, 2, 0, 3) for x in gather[step])
-        if pad > 0:
-            qv, kv, vv = (x.narrow(2, 0, x.shape[2] - pad) for x in (qv, kv, vv))
+        if async_exchange:
+            finish_fp8_exchange(pending_gathers.pop(step))
+        else:
+            acc.current_stream().wait_event(gathered[step])
+        if direct_gather:
+            qv, kv, vv = gather[step]
+        else:
+            qv, kv, vv = (x.flatten(0, 1).permute(1, 2, 0, 3) for x in gather[step])
+            if pad > 0:
+                qv, kv, vv = (x.narrow(2, 0, x.shape[2] - pad) for x in (qv, kv, vv))
         if rope_fn is not None and rotary_emb is not None and not fuse_rope:
             qv, kv = rope_fn(qv, kv, *rotary_emb)
         cs = sizes[step]
-        if getattr(attention_fn, "writes_into", False):
+        if fused_return_pack:
+            # The return encode reads the [B, cs, S, D] output as it is.
+            results[step] = attention_fn(qv, kv, vv, head_offset=offsets[step],
+                                         attn_mask=attention_mask).type_as(query)
+        elif getattr(attention_fn, "writes_into", False):
             # The kernel epilogue stores straight into the return-A2A send
             # layout (W_S, S, B, cs, D): no reshape/pad copies.
             send = torch.empty((W_S, Sq, B, cs, D), device=query.device, dtype=query.dtype)
@@ -164,16 +205,31 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             ctx = acc.stream(scatter_stream) if scatter_stream is not None else nullcontext()
             with ctx:
                 output_stream.wait_event(attended[step])
-                exchange_one(returned[step], results[step], output_group)
+                if async_exchange:
+                    pending_returns.append(submit_fp8_exchange(
+                        None if direct_return else (returned[step],), (results[step],), D,
+                        output_group, row_tiling=async_options.row_tiling,
+                        return_shard_seq=Sq if fused_return_pack else 0))
+                else:
+                    exchange_one(returned[step], results[step], output_group)
                 if device_join:
                     results[step].record_stream(comm_stream)
                     for t in chunks[step]:
                         t.record_stream(comm_stream)
 
-    if device_join:
+    if async_exchange:
+        for step, pending in zip(order, pending_returns):
+            if direct_return:
+                layout = (Sq, B, W_S, hpd, sizes[step], offsets[step])
+                finish_fp8_exchange(pending, output=final, return_layout=layout)
+            else:
+                finish_fp8_exchange(pending)
+    elif device_join:
         acc.current_stream().wait_stream(comm_stream)
     else:
         comm_stream.synchronize()
     if scatter_stream is not None:
         scatter_stream.synchronize()
+    if direct_return:
+        return final
     return torch.cat([b.permute(2, 1, 0, 3) for b in returned], dim=3).flatten(-2, -1)
