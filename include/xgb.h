@@ -186,7 +186,12 @@ int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, int64_t c
  * row-major (16-byte aligned, K and N multiples of 16); scale strides 0
  * (per-tensor scalar) or 1 (per row / per output channel); bias bf16 [N]
  * or NULL; out bf16 rows ldo elements apart. activation: 0 none, 1 GELU
- * (erf), 2 GELU (tanh approximation), applied after the bias (FFN up).
+ * (erf), 2 GELU (tanh approximation), applied after the bias (FFN up),
+ * 3 gate-first SwiGLU: w rows (and scale_w, bias) interleaved in groups of
+ * 128 as [gate j..j+127 | value j..j+127] (N % 256 == 0), and
+ *     out[m, j] = bf16(bf16(silu(yg)) * yv), yg/yv the bf16 plain results
+ * of the gate/value rows, N/2 output columns (replaces the separate
+ * gate_first_swiglu pass, x_base/x_base/operator/h3_swiglu.py:15-41).
  * When gate != NULL the AdaLN gated residual is fused in, with the
  * reference's rounding after each op:
  *     out[m, n] = bf16(bf16(y * gate[gate_index[m]*ldg + n]) + residual[m*ldr + n])
@@ -207,7 +212,9 @@ int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t N, int64
  *   h = bf16(bf16(n * bf16(1 + scale[t])) + shift[t]),  t = indices[row % seq]
  *   out = e4m3(h / s), out_scale[row] = s = max(amax|h| / 448, FLT_MIN)
  * scale/shift are bf16 table rows (strides lds/ldsh); out_bf16 (optional)
- * receives h. width <= 6144.
+ * receives h. width <= 6144. With out = out_scale = NULL (out_bf16 set) it
+ * is the final layer's output AdaLN, norm_out + modulation
+ * (x_diffusers/x_diffusers/framework/transformer/minimax_h3.py:672-696).
  * Replaces norm1/norm2 + `_apply(..., modulation=True)` of the H3 block
  * (x_base/x_base/operator/h3_indexed_affine.py:52-61,
  * x_diffusers/x_diffusers/framework/transformer/h3_npu_fusion.py:339-356)

@@ -76,3 +76,26 @@ def test_norm_modulate_quant_matches_unfused(cuda_device):
     assert (d <= bound).all()
     rc, rs = quantize_per_token(mod.reshape(b * s, h))
     assert torch.equal(scales, rs) and torch.equal(codes.view(torch.uint8), rc.view(torch.uint8))
+
+
+def test_output_adaln_matches_layernorm_then_indexed_affine(cuda_device):
+    """Final-layer norm_out (minimax_h3.py:672-696) in one pass vs torch
+    LayerNorm + the bit-exact indexed-affine kernel, and vs the bf16 copy the
+    quantising prologue writes."""
+    from xgen_b200.ops import indexed_affine, norm_modulate_quant, output_adaln
+
+    g = torch.Generator().manual_seed(5)
+    b, s, h = 1, 257, 3072
+    x = (2 * torch.randn(b, s, h, generator=g)).bfloat16().to(cuda_device)
+    shift = torch.randn(3, h, generator=g).bfloat16().to(cuda_device)
+    scale = torch.randn(3, h, generator=g).bfloat16().to(cuda_device)
+    idx = torch.randint(3, (s,), generator=g).to(cuda_device)
+    got = output_adaln(x, scale, shift, idx)
+    _, _, mod = norm_modulate_quant(x, "layernorm", None, 1e-6, scale, shift, idx, return_bf16=True)
+    assert torch.equal(got, mod)
+    n = torch.nn.functional.layer_norm(x.float(), (h,), eps=1e-6).bfloat16()
+    ref = indexed_affine(n, scale, shift, idx, modulation=True)
+    f = (1.0 + scale.index_select(0, idx).float()).bfloat16().float()
+    bound = (n.float() * f).abs() * 2 ** -7 + ref.float().abs() * 2 ** -7 + 1e-6
+    assert (got == ref).float().mean() > 0.99
+    assert ((got.float() - ref.float()).abs() <= bound).all()

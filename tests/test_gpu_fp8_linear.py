@@ -108,3 +108,29 @@ def test_gated_epilogue_matches_gemm_then_indexed_affine(cuda_device):
     plain = layer(x)
     two_step = indexed_affine(plain, gate, res, idx, modulation=False)
     assert torch.equal(fused, two_step)
+
+
+@pytest.mark.parametrize("scaling", ["per_tensor", "per_token"])
+def test_swiglu_epilogue_matches_gemm_then_swiglu(cuda_device, scaling):
+    """FFN up projection + gate-first SwiGLU (h3_swiglu.py:15-41) fused in
+    the GEMM epilogue vs the plain GEMM followed by the bit-exact SwiGLU
+    kernel: identical bits (same bf16 GEMM results, same SwiGLU rounding)."""
+    from xgen_b200.fp8_linear import H3FP8Linear
+    from xgen_b200.ops import gate_first_swiglu, quantize_per_token
+
+    g = torch.Generator().manual_seed(11)
+    m, hid, f = 389, 1024, 1536
+    w = (torch.randn(2 * f, hid, generator=g) * 0.03).bfloat16()
+    bias = torch.randn(2 * f, generator=g).bfloat16()
+    plain = H3FP8Linear(w, bias, scaling=scaling).to(cuda_device)
+    fused = plain.swiglu_interleaved()
+    x = torch.randn(m, hid, generator=g).bfloat16().to(cuda_device)
+    expect = gate_first_swiglu(plain(x))
+    got = fused(x)
+    assert got.shape == (m, f)
+    assert torch.equal(got, expect)
+    q, s = quantize_per_token(x)
+    assert torch.equal(fused.forward_quantized(q, s, activation=3),
+                       gate_first_swiglu(plain.forward_quantized(q, s)))
+    with pytest.raises(ValueError):
+        plain.forward_quantized(q, s, activation=3)

@@ -79,6 +79,17 @@ __device__ __forceinline__ bool poly_pair(int pair) {
 #define XGB_ATTN_TURN 1
 #endif
 constexpr bool kTurn = XGB_ATTN_TURN != 0;
+constexpr int kTurnBar = 1;  // named barriers 1, 2: exp turn of WG0, WG1
+// Sage with kSmemP: P goes to shared memory (SW128 K-major rows, read by an
+// SS P.V MMA) instead of over its S buffer, so the whole S buffer can be
+// preset to 0x4B400000 right after it is read: the next QK^T accumulates
+// onto that bias and S arrives as the magic float 12582912 + s with no
+// per-element integer add in the softmax.
+#ifndef XGB_ATTN_SMEM_P
+#define XGB_ATTN_SMEM_P 0
+#endif
+constexpr bool kSmemP = XGB_ATTN_SMEM_P != 0;
+constexpr uint32_t kMagic = 0x4B400000u;
 
 template <bool kSage>
 struct Cfg {
@@ -93,7 +104,10 @@ struct Cfg {
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQT * kQBytes;
   static constexpr int kVOff = kKOff + kStages * kKVBytes;
-  static constexpr int kBarOff = kVOff + kStages * kKVBytes;
+  static constexpr bool kPInSmem = kSage && kSmemP;
+  static constexpr int kPBytes = kPInSmem ? kBM * 128 : 0;  // one P buffer, 128-byte rows
+  static constexpr int kPOff = kVOff + kStages * kKVBytes;   // [Q tile][S buffer]
+  static constexpr int kBarOff = kPOff + 4 * kPBytes;
   static constexpr int kSmem = kBarOff + 512 + 1024;  // + barriers + alignment slack
   static constexpr uint32_t kIdescQK =
       kSage ? instr_desc(2, 1, 1, false, false, kBM, kBN) : instr_desc(1, 1, 1, false, false, kBM, kBN);
@@ -126,7 +140,6 @@ struct Barriers {
   uint64_t p_full[2][2];
   uint64_t pv_done[2];
   uint64_t o_done[2];  // every P.V of Q tile i has landed in O_i
-  uint64_t turn[2];    // exp-section ping-pong between the softmax warpgroups
   uint64_t end[2];
   uint32_t tmem_base;
 };
@@ -198,7 +211,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->o_done[i], 1);
       mbar_init(&bars->end[i], 1);
-      mbar_init(&bars->turn[i], kBM);
     }
     fence_barrier_init();
   }
@@ -212,6 +224,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  if constexpr (C::kPInSmem) {
+    // Preset both S buffers of each Q tile before their first QK^T.
+    if (warp < 8) {
+      const uint32_t la = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+      for (int b = 0; b < 2; ++b) {
+        tmem_st32_fill(la + s_col(warp >> 2, b), kMagic);
+        tmem_st32_fill(la + s_col(warp >> 2, b) + 32, kMagic);
+      }
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
 
   if (warp == kTmaWarp) {
     // ------------------------------------------------------------ producer
@@ -257,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < C::kKStepsD; ++k)
           mma_ss<kQK>(tmem + s_col(i, t & 1), kmajor_desc<kSage>(qa, k, kBM * 128),
-                      kmajor_desc<kSage>(ka, k, C::kSub), C::kIdescQK, k > 0);
+                      kmajor_desc<kSage>(ka, k, C::kSub), C::kIdescQK, C::kPInSmem || k > 0);
         tc_commit(&bars->s_full[i][t & 1]);
       };
       bool ok = mbar_wait(&bars->q_full, 0, p.err);
@@ -275,10 +301,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         // O_i += P_i(t) . V(t)
         const uint32_t va = v_saddr + s * C::kKVBytes;
+        if constexpr (C::kPInSmem) {
+          const uint32_t pa = smem_u32(smem + C::kPOff) + (2 * i + (t & 1)) * C::kPBytes;
 #pragma unroll
-        for (int k = 0; k < C::kKStepsN; ++k)
-          mma_ts<kPV>(tmem + o_col(i), tmem + s_col(i, t & 1) + k * 8, vdesc<kSage>(va, k),
-                      C::kIdescPV, t > 0 || k > 0);
+          for (int k = 0; k < C::kKStepsN; ++k)
+            mma_ss<kPV>(tmem + o_col(i), smem_desc_sw128(pa + k * 32, 16, 1024),
+                        vdesc<kSage>(va, k), C::kIdescPV, t > 0 || k > 0);
+        } else {
+#pragma unroll
+          for (int k = 0; k < C::kKStepsN; ++k)
+            mma_ts<kPV>(tmem + o_col(i), tmem + s_col(i, t & 1) + k * 8, vdesc<kSage>(va, k),
+                        C::kIdescPV, t > 0 || k > 0);
+        }
         tc_commit(&bars->pv_done[i]);
         tc_commit(&bars->kv_empty[s]);
         const int t2 = t + 2;
@@ -310,9 +344,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kSage) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride];
     bool ok = true;
     // The two warpgroups take turns in the MUFU-bound exp section so one's
-    // exp overlaps the other's load/max/rescale work; WG1 hands the first
-    // turn to WG0.
-    if (kTurn && i == 1) mbar_arrive(&bars->turn[0]);
+    // exp overlaps the other's load/max/rescale work. The turn passes through
+    // hardware named barriers (far cheaper to hand over than an mbarrier
+    // poll): WG i waits on barrier kTurnBar + i, which completes when its 128
+    // threads sync and the other WG's 128 arrive. WG1 hands the first turn to
+    // WG0. Every iteration makes exactly one sync and one arrive per WG (WG1
+    // skips its last arrive, which nothing would consume); a WG that stops
+    // early on a failed wait still makes its remaining ones (below), so
+    // neither WG can be left in bar.sync.
+    const int turn_own = kTurnBar + i, turn_other = kTurnBar + (i ^ 1);
+    int turns = 0;
+    if (kTurn && i == 1 && n_kv > 0) named_arrive(turn_other, 2 * kBM);
     for (int t = 0; t < n_kv; ++t) {
       const uint32_t s_addr = lane_addr + s_col(i, t & 1);
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[i][t & 1], (t >> 1) & 1, p.err));
@@ -331,10 +373,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float comb = kSage ? qs * ks : p.scale_log2;
       if constexpr (kSage) {
         if (t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + t + 1];
+        if constexpr (C::kPInSmem) {
+          // S already carries the bias; re-arm the buffer for S(t+2).
+          tmem_st32_fill(s_addr, kMagic);
+          tmem_st32_fill(s_addr + 32, kMagic);
+        } else {
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r[c][e] += 0x4B400000u;
+            for (int e = 0; e < 32; ++e) r[c][e] += kMagic;
+        }
       }
       if (valid < kBN) {
         const uint32_t sentinel = kSage ? 0x4B000000u /* 12582912 - 2^22 */ : 0xFF800000u /* -inf */;
@@ -382,10 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      if constexpr (kTurn) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->turn[i], t & 1, p.err));
-        if (!ok) break;
-      }
+      if constexpr (kTurn) named_sync(turn_own, 2 * kBM);
       // P = exp2(comb*s - m_used) (times kPScale for e4m3, folded into the
       // exponent), row sum, pack and store over the S buffer.
       // Row sums in four independent packed chains (short dependency chains).
@@ -415,7 +460,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             packed[c * 8 + e / 4] = pack_e4m3x2(pv[0], pv[1]) | (pack_e4m3x2(pv[2], pv[3]) << 16);
           }
         }
-        tmem_st16(s_addr, packed);
+        if constexpr (C::kPInSmem) {
+          // Row r of the P tile: 8-row atoms of 1024 B, 16-byte chunk c of
+          // the 128-byte row stored at chunk c ^ (r % 8) (SWIZZLE_128B).
+          const int r_loc = lane_base + lane;
+          const uint32_t prow = smem_u32(smem + C::kPOff) + (2 * i + (t & 1)) * C::kPBytes +
+                                (r_loc >> 3) * 1024 + (r_loc & 7) * 128;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch)
+            st_shared_v4(prow + ((ch ^ (r_loc & 7)) << 4), packed[4 * ch], packed[4 * ch + 1],
+                         packed[4 * ch + 2], packed[4 * ch + 3]);
+          fence_proxy_async_smem();
+        } else {
+          tmem_st16(s_addr, packed);
+        }
       } else {
         const float off = -m_used;
 #pragma unroll
@@ -439,11 +497,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(s_addr + c * 16, packed);
         }
       }
-      if constexpr (kTurn) mbar_arrive(&bars->turn[i ^ 1]);
+      if constexpr (kTurn) {
+        if (!(i == 1 && t == n_kv - 1)) named_arrive(turn_other, 2 * kBM);
+        turns = t + 1;
+      }
       l += ((rsa[0] + rsb[0]) + (rsa[1] + rsb[1])) + ((rsa[2] + rsb[2]) + (rsa[3] + rsb[3]));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->p_full[i][t & 1]);
+    }
+    if constexpr (kTurn) {
+      for (int t = turns; t < n_kv; ++t) {  // after a failed wait: keep the turn protocol
+        named_sync(turn_own, 2 * kBM);
+        if (!(i == 1 && t == n_kv - 1)) named_arrive(turn_other, 2 * kBM);
+      }
     }
     // ------------------------------------------------------------ epilogue
     // pv_done may trail the last tile by two phases here, so a parity wait

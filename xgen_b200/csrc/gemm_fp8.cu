@@ -3,6 +3,11 @@
 //   out[m, n] = bf16(acc[m, n] * (sa[m] * sb[n]) + bias[n])        (plain)
 //   out[m, n] = bf16(bf16(y * gate[idx[m], n]) + residual[m, n])    (gated)
 //       with y = the plain result, the AdaLN gate + residual of the block
+//   out[m, j] = bf16(bf16(silu(yg)) * yv)                              (SwiGLU)
+//       with yg, yv = bf16 plain results of the gate and value columns of
+//       the gate-first SwiGLU (x_base/x_base/operator/h3_swiglu.py:15-29):
+//       W rows interleaved in groups of 128, [gate j..j+127 | value
+//       j..j+127] per 256-row tile, so one tile yields 128 outputs
 //
 // acc = sum_k A[m, k] * W[n, k] in fp32 (tcgen05 kind::f8f6f4), A [M, K] and
 // W [N, K] e4m3 row-major (both K-major), sa/sb per-row/per-column scales
@@ -40,12 +45,18 @@ constexpr int kBarOff = kStages * kStageBytes;
 constexpr int kSmem = kBarOff + 256 + 1024;
 constexpr uint32_t kIdesc = instr_desc(1, 0, 0, false, false, kBM, kBN);
 
-enum Epilogue : int { kPlain = 0, kGated = 1, kGeluErf = 2, kGeluTanh = 3 };
+enum Epilogue : int { kPlain = 0, kGated = 1, kGeluErf = 2, kGeluTanh = 3, kSwiGLU = 4 };
 
 // GELU of the FFN up projection: exact (erf) or the tanh approximation.
 __device__ __forceinline__ float gelu_erf(float y) { return 0.5f * y * (1.0f + erff(y * 0.70710678118654752f)); }
 __device__ __forceinline__ float gelu_tanh(float y) {
   return 0.5f * y * (1.0f + tanhf(0.79788456080286536f * (y + 0.044715f * y * y * y)));
+}
+// Gate-first SwiGLU of one bf16 gate/value pair with the reference's
+// rounding: act = bf16(g / (1 + exp(-g))), out = bf16(act * v).
+__device__ __forceinline__ float swiglu_pair(float g, float v) {
+  const float act = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+  return bf16_round(__fmul_rn(act, v));
 }
 
 struct Params {
@@ -179,6 +190,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = m < p.M;
       const float sa = row_ok ? p.sa[m * p.sa_stride] : 0.f;
       const int64_t grow = (kEpi == kGated && row_ok) ? p.idx[m] : 0;
+      if constexpr (kEpi == kSwiGLU) {
+        // N % 256 == 0 (checked on the host): gate columns n0 + [0, 128),
+        // value columns n0 + [128, 256), outputs n0/2 + [0, 128).
+#pragma unroll 1
+        for (int c = 0; c < kBN / 64; ++c) {
+          uint32_t rg[32], rv[32];
+          tmem_ld32(lane_addr + a * kBN + c * 32, rg);
+          tmem_ld32(lane_addr + a * kBN + kBN / 2 + c * 32, rv);
+          tmem_ld_wait();
+          if (row_ok) {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float y[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int ng = n0 + c * 32 + e + u, nv = ng + kBN / 2;
+                const float bg = p.bias ? __bfloat162float(p.bias[ng]) : 0.f;
+                const float bv = p.bias ? __bfloat162float(p.bias[nv]) : 0.f;
+                const float g = bf16_round(fmaf(__uint_as_float(rg[e + u]), sa * p.sb[ng * p.sb_stride], bg));
+                const float v = bf16_round(fmaf(__uint_as_float(rv[e + u]), sa * p.sb[nv * p.sb_stride], bv));
+                y[u] = swiglu_pair(g, v);
+              }
+              w[e / 2] = pack_bf16x2(y[0], y[1]);
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m) * p.ldo + n0 / 2 + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->acc_empty[a]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
@@ -274,10 +319,12 @@ XGB_API int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t 
   if (K % 16 || N % 16) return XGB_ERR_SHAPE;  // 16-byte TMA rows, as the reference requires
   if ((scale_a_stride != 0 && scale_a_stride != 1) || (scale_w_stride != 0 && scale_w_stride != 1))
     return XGB_ERR_STRIDE;
-  if (ldo < N || ldo % 8) return XGB_ERR_STRIDE;
+  const bool swiglu = activation == 3;
+  if (swiglu && N % 256) return XGB_ERR_SHAPE;  // whole gate/value groups per tile
+  if (ldo < (swiglu ? N / 2 : N) || ldo % 8) return XGB_ERR_STRIDE;
   const bool gated = gate != nullptr;
   if (gated && (!gate_index || !residual || ldr < N || ldg < N)) return XGB_ERR_ARG;
-  if (activation < 0 || activation > 2 || (gated && activation != 0)) return XGB_ERR_ARG;
+  if (activation < 0 || activation > 3 || (gated && activation != 0)) return XGB_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) |
        reinterpret_cast<uintptr_t>(out)) & 15u)
     return XGB_ERR_ALIGN;
@@ -307,5 +354,6 @@ XGB_API int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t 
   if (gated) return gemm::launch<gemm::kGated>(a, w, p, st);
   if (activation == 1) return gemm::launch<gemm::kGeluErf>(a, w, p, st);
   if (activation == 2) return gemm::launch<gemm::kGeluTanh>(a, w, p, st);
+  if (activation == 3) return gemm::launch<gemm::kSwiGLU>(a, w, p, st);
   return gemm::launch<gemm::kPlain>(a, w, p, st);
 }

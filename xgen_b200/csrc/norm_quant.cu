@@ -9,7 +9,9 @@
 // (x_base/x_base/operator/h3_indexed_affine.py:52-61, h3_npu_fusion.py:339-356)
 // followed by the activation quantisation of the next FP8 Linear, in one HBM
 // pass: read 2 B and write 1 B per element (+ an optional bf16 copy of h).
-// One CTA per row; the row stays in registers between the passes.
+// One CTA per row; the row stays in registers between the passes. With no
+// e4m3 output it is the final layer's output AdaLN, norm_out + modulation
+// (x_diffusers/x_diffusers/framework/transformer/minimax_h3.py:672-696).
 #include <cfloat>
 
 #include "xgb_common.cuh"
@@ -91,6 +93,14 @@ __global__ void __launch_bounds__(kThreads) norm_modulate_quant_kernel(
       amax = fmaxf(amax, fabsf(h));
     }
   }
+  if (out_bf16) {
+#pragma unroll
+    for (int j = 0; j < kMaxPerThread; ++j) {
+      const int c = threadIdx.x + j * kThreads;
+      if (c < width) out_bf16[row * static_cast<int64_t>(width) + c] = __float2bfloat16_rn(v[j]);
+    }
+  }
+  if (!out) return;  // modulation only (the final layer's output AdaLN)
   amax = block_max(amax, red);
   const float sc = fmaxf(__fdiv_rn(amax, 448.0f), FLT_MIN);
   if (threadIdx.x == 0) out_scale[row] = sc;
@@ -98,10 +108,7 @@ __global__ void __launch_bounds__(kThreads) norm_modulate_quant_kernel(
 #pragma unroll
   for (int j = 0; j < kMaxPerThread; ++j) {
     const int c = threadIdx.x + j * kThreads;
-    if (c < width) {
-      orow[c] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(v[j], sc), -448.f), 448.f));
-      if (out_bf16) out_bf16[row * static_cast<int64_t>(width) + c] = __float2bfloat16_rn(v[j]);
-    }
+    if (c < width) orow[c] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(v[j], sc), -448.f), 448.f));
   }
 }
 
@@ -115,7 +122,8 @@ XGB_API int xgb_norm_modulate_quant(const void* x, int64_t ldx, int64_t rows, in
                                     const void* scale, int64_t lds, const void* shift,
                                     int64_t ldsh, const int64_t* indices, uint8_t* out,
                                     float* out_scale, void* out_bf16, void* stream) {
-  if (!x || !scale || !shift || !indices || !out || !out_scale) return XGB_ERR_ARG;
+  if (!x || !scale || !shift || !indices) return XGB_ERR_ARG;
+  if ((out == nullptr) != (out_scale == nullptr) || (!out && !out_bf16)) return XGB_ERR_ARG;
   if (rows < 0 || width <= 0 || width > kThreads * kMaxPerThread || seq <= 0 || rows % seq)
     return XGB_ERR_SHAPE;
   if (ldx < width || lds < width || ldsh < width) return XGB_ERR_STRIDE;

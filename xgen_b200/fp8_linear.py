@@ -13,6 +13,9 @@ schemes:
 
 `forward_gated` fuses the AdaLN gated residual that follows the attention and
 FFN output projections (h3_indexed_affine.py:52-61) into the GEMM epilogue.
+`swiglu_interleaved()` returns a copy of a gate-first SwiGLU up projection
+whose rows are regrouped so that the GEMM epilogue applies the SwiGLU
+(h3_swiglu.py:15-41) and writes only the [M, out/2] activation.
 """
 from __future__ import annotations
 
@@ -57,6 +60,7 @@ class H3FP8Linear(nn.Module):
         self.register_buffer("weight_scale", scale.reshape(-1).float())
         self.register_buffer("bias", bias.detach().clone().to(torch.bfloat16) if bias is not None else None)
         self.calls = 0
+        self.swiglu = False
 
     @classmethod
     def from_packed(cls, weight, scale, bias=None):
@@ -73,6 +77,31 @@ class H3FP8Linear(nn.Module):
         result.register_buffer("weight_scale", scale.detach().clone().reshape(1))
         result.register_buffer("bias", bias.detach().clone().to(torch.bfloat16) if bias is not None else None)
         result.calls = 0
+        result.swiglu = False
+        return result
+
+    def swiglu_interleaved(self) -> "H3FP8Linear":
+        """The same projection with rows regrouped per 128 as [gate j..j+127 |
+        value j..j+127] (gate = the first out/2 rows), for the fused SwiGLU
+        epilogue; its forward_quantized(..., activation=3) returns
+        silu(gate) * value with the reference's bf16 rounding."""
+        half = self.out_features // 2
+        if self.out_features % 256:
+            raise ValueError("fused SwiGLU needs out_features divisible by 256")
+        order = torch.arange(self.out_features, device=self.weight.device).view(2, half // 128, 128)
+        order = order.permute(1, 0, 2).reshape(-1)
+        result = self.__class__.__new__(self.__class__)
+        nn.Module.__init__(result)
+        result.scaling = self.scaling
+        result.out_features, result.in_features = self.out_features, self.in_features
+        result.register_buffer("weight", self.weight.index_select(0, order).contiguous())
+        scale = self.weight_scale
+        result.register_buffer("weight_scale", scale.index_select(0, order) if scale.numel() > 1
+                               else scale.clone())
+        result.register_buffer("bias", self.bias.index_select(0, order)
+                               if self.bias is not None else None)
+        result.calls = 0
+        result.swiglu = True
         return result
 
     def _check(self, x):
@@ -103,26 +132,36 @@ class H3FP8Linear(nn.Module):
     def forward_quantized(self, q, scale, activation: int = 0, gated=None, out_shape=None):
         """GEMM on activations already quantised to e4m3 (q [M, in], scale
         [M] per token or [1] per tensor), e.g. by the fused norm/modulate/
-        quant prologue. activation: 0 none, 1 GELU (erf), 2 GELU (tanh)."""
+        quant prologue. activation: 0 none, 1 GELU (erf), 2 GELU (tanh),
+        3 gate-first SwiGLU (only on a `swiglu_interleaved()` projection;
+        the result has out_features/2 columns)."""
         if q.dtype != torch.float8_e4m3fn or q.ndim != 2 or q.shape[1] != self.in_features:
             raise ValueError("pre-quantised FP8 Linear input must be e4m3 [M, in]")
+        if (activation == 3) != self.swiglu:
+            raise ValueError("the fused SwiGLU needs (and only fits) a swiglu_interleaved projection")
         m = q.shape[0]
+        width = self.out_features // 2 if activation == 3 else self.out_features
         return self._gemm(q.contiguous(), scale.reshape(-1), 1 if scale.numel() > 1 else 0, m,
-                          q.device, activation, gated, out_shape or (m, self.out_features))
+                          q.device, activation, gated, out_shape or (m, width))
 
     def _forward(self, x, gated):
         self._check(x)
         matrix = x.reshape(-1, self.in_features)
         m = matrix.shape[0]
+        # A swiglu_interleaved projection always applies its SwiGLU.
+        activation, width = (3, self.out_features // 2) if self.swiglu else (0, self.out_features)
+        if gated is not None and self.swiglu:
+            raise ValueError("the gated epilogue does not combine with the fused SwiGLU")
         if not m:
-            return x.new_empty((*x.shape[:-1], self.out_features))
+            return x.new_empty((*x.shape[:-1], width))
         matrix = matrix.contiguous()
         q, sa, sa_stride = self._quantize(matrix)
-        out = self._gemm(q, sa, sa_stride, m, x.device, 0, gated, (*x.shape[:-1], self.out_features))
+        out = self._gemm(q, sa, sa_stride, m, x.device, activation, gated, (*x.shape[:-1], width))
         return out if x.dtype == torch.bfloat16 else out.to(x.dtype)
 
     def _gemm(self, q, sa, sa_stride, m, device, activation, gated, out_shape):
-        out = torch.empty((m, self.out_features), device=device, dtype=torch.bfloat16)
+        width = self.out_features // 2 if activation == 3 else self.out_features
+        out = torch.empty((m, width), device=device, dtype=torch.bfloat16)
         gate = idx = res = None
         ldg = ldr = 0
         if gated is not None:
@@ -139,7 +178,7 @@ class H3FP8Linear(nn.Module):
              self.in_features, sa.data_ptr(), sa_stride, self.weight_scale.data_ptr(),
              0 if self.weight_scale.numel() == 1 else 1,
              self.bias.data_ptr() if self.bias is not None else None, activation, out.data_ptr(),
-             self.out_features, gate.data_ptr() if gate is not None else None, ldg,
+             width, gate.data_ptr() if gate is not None else None, ldg,
              idx.data_ptr() if idx is not None else None,
              res.data_ptr() if res is not None else None, ldr, _err_flag(device).data_ptr(),
              torch.cuda.current_stream(device).cuda_stream)

@@ -58,6 +58,11 @@ class H3DiTBlockB200:
         self.to_qkv = lin("to_qkv")
         self.to_out = lin("to_out")
         self.ff_up = lin("ff_up")
+        # Gate-first SwiGLU fused into the up projection's epilogue when its
+        # gate/value halves tile evenly (2F % 256 == 0).
+        self.fused_swiglu = c.activation == "swiglu" and self.ff_up.out_features % 256 == 0
+        if self.fused_swiglu:
+            self.ff_up = self.ff_up.swiglu_interleaved()
         self.ff_down = lin("ff_down")
         self.norm1_weight = weights.get("norm1.weight")
         self.norm2_weight = weights.get("norm2.weight")
@@ -121,6 +126,8 @@ class H3DiTBlockB200:
             a, sa = norm_modulate_quant(x, c.norm, self.norm2_weight, c.eps, scale_ff, shift_ff, idx)
             if c.activation == "gelu":
                 hid = self.ff_up.forward_quantized(a, sa, activation=1)
+            elif self.fused_swiglu:
+                hid = self.ff_up.forward_quantized(a, sa, activation=3)
             else:
                 hid = gate_first_swiglu(self.ff_up.forward_quantized(a, sa))
             hq, hs = quantize_per_token(hid)

@@ -168,6 +168,28 @@ def norm_modulate_quant(x: torch.Tensor, norm: str, weight, eps: float, scale: t
     return (codes, scales, mod) if return_bf16 else (codes, scales)
 
 
+def output_adaln(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                 indices: torch.Tensor, *, norm: str = "layernorm", weight=None,
+                 eps: float = 1e-6) -> torch.Tensor:
+    """Final-layer output AdaLN of the H3 transformer (`norm_out`:
+    x_diffusers/x_diffusers/framework/transformer/minimax_h3.py:672-696):
+    bf16(bf16(norm(x) * bf16(1 + scale[idx])) + shift[idx]) in one pass;
+    scale/shift are the [M, H] tables of lookup_final()."""
+    _require_cuda(x, scale, shift, indices, what="H3 output AdaLN")
+    if (x.ndim != 3 or x.dtype != torch.bfloat16 or x.stride(-1) != 1 or x.stride(0) != x.shape[1] * x.stride(1)
+            or scale.dtype != torch.bfloat16 or shift.dtype != torch.bfloat16
+            or scale.stride(-1) != 1 or shift.stride(-1) != 1 or indices.dtype != torch.int64
+            or indices.numel() != x.shape[1] or norm not in ("layernorm", "rmsnorm")):
+        raise ValueError("output_adaln needs bf16 [B,S,H] rows, bf16 tables, int64 [S] indices")
+    b, s, h = x.shape
+    out = torch.empty((b, s, h), device=x.device, dtype=torch.bfloat16)
+    call("xgb_norm_modulate_quant", x.data_ptr(), x.stride(1), b * s, h, s,
+         1 if norm == "rmsnorm" else 0, weight.data_ptr() if weight is not None else None,
+         float(eps), scale.data_ptr(), scale.stride(0), shift.data_ptr(), shift.stride(0),
+         indices.contiguous().data_ptr(), None, None, out.data_ptr(), _stream(x))
+    return out
+
+
 def quantize_per_token(x: torch.Tensor):
     """Per-row dynamic e4m3 of a 2-D bf16/fp16 matrix: (codes, scales[rows])."""
     _require_cuda(x, what="H3 FP8 quantization")
