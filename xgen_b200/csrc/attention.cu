@@ -55,21 +55,13 @@ constexpr int kMmaWarp = 9;  // warps 9 and 10 issue the MMAs of Q tiles 0 and 1
 constexpr float kNegInf = -__builtin_huge_valf();
 // log2(448 / 2^4): e4m3 P = exp2(x + kLog2PScale) spans up to 448 under kTau = 4.
 constexpr float kLog2PScale = 4.807354922057604f;
-// With kPolyEvery > 0, one exp2 in kPolyEvery goes to the FMA pipe
-// (ex2_poly) instead of MUFU. Measured on B200 at this tile shape it only
-// adds issue pressure (MUFU is not the limiter once the exp sections
-// ping-pong), so it is off by default.
-#ifndef XGB_ATTN_POLY_EVERY
-#define XGB_ATTN_POLY_EVERY 0
-#endif
-constexpr int kPolyEvery = XGB_ATTN_POLY_EVERY;
-__device__ __forceinline__ bool use_poly(int idx) {
-  return kPolyEvery > 0 && idx % (kPolyEvery > 0 ? kPolyEvery : 1) == kPolyEvery - 1;
-}
-// With kPolyPairs > 0, one pair of exp2 in kPolyPairs runs as a packed
-// fp32x2 polynomial (ex2_poly2) instead of two MUFU ops.
+// One pair of exp2 in kPolyPairs runs as a packed fp32x2 polynomial
+// (ex2_poly2) on the FMA pipe instead of two MUFU ops in the Sage kernel,
+// easing the MUFU load of the exp section a little: measured on B200, 1 in 8
+// pairs gains ~2 % (768P-5s); larger shares lose, because the exp section is bound by
+// issue and latency rather than by MUFU throughput. 0 disables it.
 #ifndef XGB_ATTN_POLY_PAIRS
-#define XGB_ATTN_POLY_PAIRS 0
+#define XGB_ATTN_POLY_PAIRS 8
 #endif
 constexpr int kPolyPairs = XGB_ATTN_POLY_PAIRS;
 __device__ __forceinline__ bool poly_pair(int pair) {
@@ -80,15 +72,6 @@ __device__ __forceinline__ bool poly_pair(int pair) {
 #endif
 constexpr bool kTurn = XGB_ATTN_TURN != 0;
 constexpr int kTurnBar = 1;  // named barriers 1, 2: exp turn of WG0, WG1
-// Sage with kSmemP: P goes to shared memory (SW128 K-major rows, read by an
-// SS P.V MMA) instead of over its S buffer, so the whole S buffer can be
-// preset to 0x4B400000 right after it is read: the next QK^T accumulates
-// onto that bias and S arrives as the magic float 12582912 + s with no
-// per-element integer add in the softmax.
-#ifndef XGB_ATTN_SMEM_P
-#define XGB_ATTN_SMEM_P 0
-#endif
-constexpr bool kSmemP = XGB_ATTN_SMEM_P != 0;
 constexpr uint32_t kMagic = 0x4B400000u;
 
 template <bool kSage>
@@ -104,10 +87,7 @@ struct Cfg {
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQT * kQBytes;
   static constexpr int kVOff = kKOff + kStages * kKVBytes;
-  static constexpr bool kPInSmem = kSage && kSmemP;
-  static constexpr int kPBytes = kPInSmem ? kBM * 128 : 0;  // one P buffer, 128-byte rows
-  static constexpr int kPOff = kVOff + kStages * kKVBytes;   // [Q tile][S buffer]
-  static constexpr int kBarOff = kPOff + 4 * kPBytes;
+  static constexpr int kBarOff = kVOff + kStages * kKVBytes;
   static constexpr int kSmem = kBarOff + 512 + 1024;  // + barriers + alignment slack
   static constexpr uint32_t kIdescQK =
       kSage ? instr_desc(2, 1, 1, false, false, kBM, kBN) : instr_desc(1, 1, 1, false, false, kBM, kBN);
@@ -224,21 +204,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  if constexpr (C::kPInSmem) {
-    // Preset both S buffers of each Q tile before their first QK^T.
-    if (warp < 8) {
-      const uint32_t la = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-      for (int b = 0; b < 2; ++b) {
-        tmem_st32_fill(la + s_col(warp >> 2, b), kMagic);
-        tmem_st32_fill(la + s_col(warp >> 2, b) + 32, kMagic);
-      }
-      tmem_st_wait();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-  }
-
   if (warp == kTmaWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -283,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < C::kKStepsD; ++k)
           mma_ss<kQK>(tmem + s_col(i, t & 1), kmajor_desc<kSage>(qa, k, kBM * 128),
-                      kmajor_desc<kSage>(ka, k, C::kSub), C::kIdescQK, C::kPInSmem || k > 0);
+                      kmajor_desc<kSage>(ka, k, C::kSub), C::kIdescQK, k > 0);
         tc_commit(&bars->s_full[i][t & 1]);
       };
       bool ok = mbar_wait(&bars->q_full, 0, p.err);
@@ -301,18 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         // O_i += P_i(t) . V(t)
         const uint32_t va = v_saddr + s * C::kKVBytes;
-        if constexpr (C::kPInSmem) {
-          const uint32_t pa = smem_u32(smem + C::kPOff) + (2 * i + (t & 1)) * C::kPBytes;
 #pragma unroll
-          for (int k = 0; k < C::kKStepsN; ++k)
-            mma_ss<kPV>(tmem + o_col(i), smem_desc_sw128(pa + k * 32, 16, 1024),
-                        vdesc<kSage>(va, k), C::kIdescPV, t > 0 || k > 0);
-        } else {
-#pragma unroll
-          for (int k = 0; k < C::kKStepsN; ++k)
-            mma_ts<kPV>(tmem + o_col(i), tmem + s_col(i, t & 1) + k * 8, vdesc<kSage>(va, k),
-                        C::kIdescPV, t > 0 || k > 0);
-        }
+        for (int k = 0; k < C::kKStepsN; ++k)
+          mma_ts<kPV>(tmem + o_col(i), tmem + s_col(i, t & 1) + k * 8, vdesc<kSage>(va, k),
+                      C::kIdescPV, t > 0 || k > 0);
         tc_commit(&bars->pv_done[i]);
         tc_commit(&bars->kv_empty[s]);
         const int t2 = t + 2;
@@ -373,16 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float comb = kSage ? qs * ks : p.scale_log2;
       if constexpr (kSage) {
         if (t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + t + 1];
-        if constexpr (C::kPInSmem) {
-          // S already carries the bias; re-arm the buffer for S(t+2).
-          tmem_st32_fill(s_addr, kMagic);
-          tmem_st32_fill(s_addr + 32, kMagic);
-        } else {
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[c][e] += kMagic;
-        }
+          for (int e = 0; e < 32; ++e) r[c][e] += kMagic;
       }
       if (valid < kBN) {
         const uint32_t sentinel = kSage ? 0x4B000000u /* 12582912 - 2^22 */ : 0xFF800000u /* -inf */;
@@ -450,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (poly_pair((c * 32 + e + u) / 2)) {
                 ex2_poly2<2>(pv[u], pv[u + 1], x[u], x[u + 1]);
               } else {
-                pv[u] = use_poly(e + u) ? ex2_poly(x[u]) : ex2_approx(x[u]);
-                pv[u + 1] = use_poly(e + u + 1) ? ex2_poly(x[u + 1]) : ex2_approx(x[u + 1]);
+                pv[u] = ex2_approx(x[u]);
+                pv[u + 1] = ex2_approx(x[u + 1]);
               }
             }
             const int ch = (e / 4) & 1;
@@ -460,20 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             packed[c * 8 + e / 4] = pack_e4m3x2(pv[0], pv[1]) | (pack_e4m3x2(pv[2], pv[3]) << 16);
           }
         }
-        if constexpr (C::kPInSmem) {
-          // Row r of the P tile: 8-row atoms of 1024 B, 16-byte chunk c of
-          // the 128-byte row stored at chunk c ^ (r % 8) (SWIZZLE_128B).
-          const int r_loc = lane_base + lane;
-          const uint32_t prow = smem_u32(smem + C::kPOff) + (2 * i + (t & 1)) * C::kPBytes +
-                                (r_loc >> 3) * 1024 + (r_loc & 7) * 128;
-#pragma unroll
-          for (int ch = 0; ch < 4; ++ch)
-            st_shared_v4(prow + ((ch ^ (r_loc & 7)) << 4), packed[4 * ch], packed[4 * ch + 1],
-                         packed[4 * ch + 2], packed[4 * ch + 3]);
-          fence_proxy_async_smem();
-        } else {
-          tmem_st16(s_addr, packed);
-        }
+        tmem_st16(s_addr, packed);
       } else {
         const float off = -m_used;
 #pragma unroll
@@ -483,13 +421,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; e += 2) {
             float xa, xb;
             ffma2(xa, xb, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb, off, off);
-            float a, b;
-            if (poly_pair((c * 32 + e) / 2)) {
-              ex2_poly2<3>(a, b, xa, xb);
-            } else {
-              a = ex2_approx(xa);
-              b = use_poly(e + 1) ? ex2_poly(xb) : ex2_approx(xb);
-            }
+            const float a = ex2_approx(xa);  // (the polynomial share does not pay for BF16)
+            const float b = ex2_approx(xb);
             const int ch = (e / 2) & 3;
             fadd2(rsa[ch], rsb[ch], rsa[ch], rsb[ch], a, b);
             packed[e / 2] = pack_bf16x2(a, b);

@@ -268,25 +268,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                : "memory");
 }
 
-// Store the same 32-bit value into 32 consecutive columns of this warp's
-// 32 TMEM lanes.
-__device__ __forceinline__ void tmem_st32_fill(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
-      " {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1,"
-      " %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
-
-// 16-byte shared-memory store (generic proxy).
-__device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c),
-               "r"(d)
-               : "memory");
-}
-
 // Hardware named barriers (ids 1..15; 0 is __syncthreads): `count` threads,
 // a multiple of 32, complete one generation. named_arrive does not wait.
 __device__ __forceinline__ void named_sync(int id, int count) {
@@ -294,12 +275,6 @@ __device__ __forceinline__ void named_sync(int id, int count) {
 }
 __device__ __forceinline__ void named_arrive(int id, int count) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// Make this thread's generic-proxy shared-memory writes visible to the async
-// proxy (tensor-core operand reads) before it signals the consumer.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -323,22 +298,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA/ALU pipes (no MUFU): x = n + f with n = round(x) and
-// f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted here to minimise
-// the maximum relative error on that interval (7.5e-5, far below the bf16 /
-// e4m3 precision of the P it feeds); 2^n added into the exponent field.
-// Inputs below -126 (and -inf) return ~2^-126.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = __fadd_rn(x, 12582912.0f);  // 1.5 * 2^23: rounds x to an integer
-  const int n = __float_as_int(t) - 0x4B400000;
-  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
-  float p = fmaf(f, 0.0551716573536396f, 0.2426111251115799f);
-  p = fmaf(f, p, 0.6932609677314758f);
-  p = fmaf(f, p, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 // max(a, b, c) in one instruction (sm_100 three-input max).
