@@ -50,7 +50,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--precision", choices=("sage", "bf16"), default="sage")
-    ap.add_argument("--phaa-num", type=int, default=2)
+    # One head chunk: measured on B200 (768P-5s, Sage), a single FP8 exchange
+    # per direction beats PHAA's chunked overlap at SP2 (71.7 vs 75.4 ms per
+    # layer) and SP8 (19.3 vs 19.5 ms): the NCCL kernels overlapping the
+    # one-CTA-per-SM attention kernel slow it more than they hide, and
+    # chunks of 3 heads quantize to 10.05 waves of 148 SMs.
+    ap.add_argument("--phaa-num", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-block", action="store_true", help="skip the full DiT block timing")

@@ -57,6 +57,27 @@ inline Workspace carve(void* ws, int64_t bh, int64_t chunks) {
   return w;
 }
 
+// Eight consecutive channels as fp32 from one 16-byte load.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) x[j] = tf<T>(e[j]);
+}
+
+// a / b correctly rounded, for a divisor shared by many quotients: with
+// y = RN(1/b), q = RN(a*y) and the exact remainder r = a - b*q (one FMA),
+// RN(q + r*y) is the correctly rounded quotient (Markstein's correction,
+// P. Markstein, IBM J. Res. Dev. 34(1), 1990) for normal b and quotient.
+__device__ __forceinline__ float div_by(float a, float b, float y) {
+  const float q = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q, b, a);
+  return __fmaf_rn(r, y, q);
+}
+
+// Per 512-row chunk of one head: channel sums of K and channel abs-max of V.
+// Thread t owns channels 8*(t%16)..+8 of rows t/16 + 16*i (16-byte loads).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) stats_kernel(const T* __restrict__ k, Strides ks,
                                                          const T* __restrict__ v, Strides vs,
@@ -64,25 +85,48 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const T* __restrict__ k
                                                          Workspace w, int64_t chunks) {
   const int64_t bh = blockIdx.y;
   const int64_t b = bh / heads, h = bh % heads;
-  const int c = threadIdx.x % kD;
-  const int r0 = threadIdx.x / kD;  // 0 or 1
+  const int cg = threadIdx.x % 16;
+  const int rr = threadIdx.x / 16;
+  const int c0 = cg * 8;
   const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * kStatsRows;
   const int64_t row_end = min(row_begin + kStatsRows, seq);
-  const T* kp = k + b * ks.b + h * ks.h + c;
-  const T* vp = v + b * vs.b + h * vs.h + c;
-  float sum = 0.f;
-  int vmax = 0;
-  for (int64_t r = row_begin + r0; r < row_end; r += 2) {
-    sum += tf<T>(kp[r * ks.s]);
-    vmax = max(vmax, __float_as_int(fabsf(tf<T>(vp[r * vs.s]))));
+  const T* kp = k + b * ks.b + h * ks.h + c0;
+  const T* vp = v + b * vs.b + h * vs.h + c0;
+  float sum[8], vmx[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    sum[j] = 0.f;
+    vmx[j] = 0.f;
   }
-  __shared__ float part[kThreads];
-  part[threadIdx.x] = sum;
+  for (int64_t r = row_begin + rr; r < row_end; r += kThreads / 16) {
+    float kx[8], vx[8];
+    load8<T>(kp + r * ks.s, kx);
+    load8<T>(vp + r * vs.s, vx);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sum[j] += kx[j];
+      vmx[j] = fmaxf(vmx[j], fabsf(vx[j]));
+    }
+  }
+  __shared__ float part[kThreads / 16][kD];
+  __shared__ float vpart[kThreads / 16][kD];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    part[rr][c0 + j] = sum[j];
+    vpart[rr][c0 + j] = vmx[j];
+  }
   __syncthreads();
-  if (r0 == 0) {
-    w.ksum[(bh * chunks + blockIdx.x) * kD + c] = part[c] + part[c + kD];
+  if (threadIdx.x < kD) {
+    const int c = threadIdx.x;
+    float t = 0.f, m = 0.f;
+#pragma unroll
+    for (int i = 0; i < kThreads / 16; ++i) {
+      t += part[i][c];
+      m = fmaxf(m, vpart[i][c]);
+    }
+    w.ksum[(bh * chunks + blockIdx.x) * kD + c] = t;
+    atomicMax(&w.vmax[bh * kD + c], __float_as_int(m));
   }
-  atomicMax(&w.vmax[bh * kD + c], vmax);
 }
 
 __global__ void __launch_bounds__(kD) finalize_kernel(Workspace w, int64_t chunks, int64_t seq,
@@ -96,8 +140,41 @@ __global__ void __launch_bounds__(kD) finalize_kernel(Workspace w, int64_t chunk
   v_scale[bh * kD + c] = fmaxf(s, FLT_MIN);
 }
 
+// Block abs-max over the CTA (256 threads).
+__device__ __forceinline__ float block_absmax(float a, float* red) {
+  a = warp_max(a);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+  __syncthreads();
+  float r = 0.f;
+#pragma unroll
+  for (int i = 0; i < kThreads / 32; ++i) r = fmaxf(r, red[i]);
+  __syncthreads();
+  return r;
+}
+
+// 4 rows x 8 channels of int8 codes round(x / s) clamped to +-127.
+__device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, const float (&x)[4][8],
+                                           float s, float y) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t w[2];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int code = __float2int_rn(div_by(x[i][half * 4 + j], s, y));
+        word |= (static_cast<uint32_t>(max(-127, min(127, code))) & 0xFFu) << (8 * j);
+      }
+      w[half] = word;
+    }
+    *reinterpret_cast<uint2*>(dst + 16 * i * row_stride) = make_uint2(w[0], w[1]);
+  }
+}
+
 // One CTA per (64-row block, head); thread t owns channels 8*(t%16)..+8 of
-// rows t/16 + 16*i, i < 4.
+// rows t/16 + 16*i, i < 4 (16-byte loads of 8 channels). Q, K and V are
+// processed one after another so few values are live (several CTAs per SM).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) quant_kernel(
     const T* __restrict__ q, Strides qs, const T* __restrict__ k, Strides ks,
@@ -111,84 +188,86 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
   const int cg = threadIdx.x % 16;
   const int rr = threadIdx.x / 16;
   const int c0 = cg * 8;
-  __shared__ float red[2][kThreads / 32];
+  const int64_t row0 = blk * 64 + rr;
+  const int64_t off0 = (bh * s_pad + row0) * kD + c0;
+  __shared__ float red[kThreads / 32];
+  float x[4][8];
 
-  float qv[4][8], kv[4][8], vv[4][8];
-  float qa = 0.f, ka = 0.f;
-  float mean[8], vsc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    mean[j] = w.kmean[bh * kD + c0 + j];
-    vsc[j] = v_scale[bh * kD + c0 + j];
-  }
+  // Q: x * sm_scale * log2(e), per-block int8.
+  float a = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int64_t row = blk * 64 + rr + 16 * i;
-    const bool live = row < seq;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      qv[i][j] = 0.f;
-      kv[i][j] = 0.f;
-      vv[i][j] = 0.f;
-    }
-    if (live) {
-      const T* qp = q + b * qs.b + h * qs.h + row * qs.s + c0;
-      const T* kp = k + b * ks.b + h * ks.h + row * ks.s + c0;
-      const T* vp = v + b * vs.b + h * vs.h + row * vs.s + c0;
+    const int64_t row = row0 + 16 * i;
+    if (row < seq) {
+      load8<T>(q + b * qs.b + h * qs.h + row * qs.s + c0, x[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        qv[i][j] = __fmul_rn(tf<T>(qp[j]), q_mult);
-        kv[i][j] = __fsub_rn(tf<T>(kp[j]), mean[j]);
-        vv[i][j] = tf<T>(vp[j]);
-        qa = fmaxf(qa, fabsf(qv[i][j]));
-        ka = fmaxf(ka, fabsf(kv[i][j]));
+        x[i][j] = __fmul_rn(x[i][j], q_mult);
+        a = fmaxf(a, fabsf(x[i][j]));
       }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
     }
   }
-  qa = warp_max(qa);
-  ka = warp_max(ka);
-  if ((threadIdx.x & 31) == 0) {
-    red[0][threadIdx.x >> 5] = qa;
-    red[1][threadIdx.x >> 5] = ka;
-  }
-  __syncthreads();
-  qa = 0.f;
-  ka = 0.f;
+  a = block_absmax(a, red);
+  float sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
+  if (threadIdx.x == 0) q_scale[bh * (s_pad / 64) + blk] = sc;
+  store_int8(q8 + off0, kD, x, sc, __frcp_rn(sc));
+
+  // K: x - mean over the sequence, per-block int8.
+  float mean[8];
 #pragma unroll
-  for (int i = 0; i < kThreads / 32; ++i) {
-    qa = fmaxf(qa, red[0][i]);
-    ka = fmaxf(ka, red[1][i]);
+  for (int j = 0; j < 8; ++j) mean[j] = w.kmean[bh * kD + c0 + j];
+  a = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = row0 + 16 * i;
+    if (row < seq) {
+      load8<T>(k + b * ks.b + h * ks.h + row * ks.s + c0, x[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        x[i][j] = __fsub_rn(x[i][j], mean[j]);
+        a = fmaxf(a, fabsf(x[i][j]));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
+    }
   }
-  const float qsc = qa > 0.f ? __fdiv_rn(qa, 127.0f) : 1.0f;
-  const float ksc = ka > 0.f ? __fdiv_rn(ka, 127.0f) : 1.0f;
-  if (threadIdx.x == 0) {
-    q_scale[bh * (s_pad / 64) + blk] = qsc;
-    k_scale[bh * (s_pad / 64) + blk] = ksc;
+  a = block_absmax(a, red);
+  sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
+  if (threadIdx.x == 0) k_scale[bh * (s_pad / 64) + blk] = sc;
+  store_int8(k8 + off0, kD, x, sc, __frcp_rn(sc));
+
+  // V: per-channel e4m3.
+  float vsc[8], vrc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    vsc[j] = v_scale[bh * kD + c0 + j];
+    vrc[j] = __frcp_rn(vsc[j]);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int64_t row = blk * 64 + rr + 16 * i;
-    const int64_t off = (bh * s_pad + row) * kD + c0;
-    uint32_t qw[2], kw[2], vw[2];
+    const int64_t row = row0 + 16 * i;
+    if (row < seq) {
+      load8<T>(v + b * vs.b + h * vs.h + row * vs.s + c0, x[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
+    }
+    uint32_t vw[2];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      uint32_t qb = 0, kb = 0, vb = 0;
+      uint32_t word = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int jj = half * 4 + j;
-        const int qi = __float2int_rn(__fdiv_rn(qv[i][jj], qsc));
-        const int ki = __float2int_rn(__fdiv_rn(kv[i][jj], ksc));
-        qb |= (static_cast<uint32_t>(max(-127, min(127, qi))) & 0xFFu) << (8 * j);
-        kb |= (static_cast<uint32_t>(max(-127, min(127, ki))) & 0xFFu) << (8 * j);
-        vb |= static_cast<uint32_t>(f32_to_e4m3(__fdiv_rn(vv[i][jj], vsc[jj]))) << (8 * j);
+        word |= static_cast<uint32_t>(f32_to_e4m3(div_by(x[i][jj], vsc[jj], vrc[jj]))) << (8 * j);
       }
-      qw[half] = qb;
-      kw[half] = kb;
-      vw[half] = vb;
+      vw[half] = word;
     }
-    *reinterpret_cast<uint2*>(q8 + off) = make_uint2(qw[0], qw[1]);
-    *reinterpret_cast<uint2*>(k8 + off) = make_uint2(kw[0], kw[1]);
-    *reinterpret_cast<uint2*>(v8 + off) = make_uint2(vw[0], vw[1]);
+    *reinterpret_cast<uint2*>(v8 + off0 + 16 * i * kD) = make_uint2(vw[0], vw[1]);
   }
 }
 
@@ -216,6 +295,12 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
   if (batch <= 0 || heads <= 0 || seq <= 0) return XGB_ERR_SHAPE;
   if (!(sm_scale > 0.f)) return XGB_ERR_ARG;
   if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1) return XGB_ERR_STRIDE;
+  // 16-byte loads of 8 channels: row starts and strides in multiples of 8.
+  for (int d = 0; d < 3; ++d)
+    if (q_strides[d] % 8 || k_strides[d] % 8 || v_strides[d] % 8) return XGB_ERR_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v)) & 15u)
+    return XGB_ERR_ALIGN;
   if ((reinterpret_cast<uintptr_t>(q8) | reinterpret_cast<uintptr_t>(k8) |
        reinterpret_cast<uintptr_t>(v8)) & 15u)
     return XGB_ERR_ALIGN;
