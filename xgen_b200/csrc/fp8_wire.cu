@@ -19,6 +19,9 @@
 //
 // Work split: a group of G = next_pow2(width/8) lanes owns one row, each lane
 // 8 channels; 32/G rows per warp, so width=128 uses full warps (2 rows each).
+#include <climits>
+#include <type_traits>
+
 #include "xgb_common.cuh"
 
 namespace xgb {
@@ -31,6 +34,7 @@ struct EncodeArgs {
   const void* src[kMaxStreams];
   int64_t st[kMaxStreams][4];  // element strides: peer, seq, batch, head
   int64_t peers, seq, batch, heads, width, rows, peer_rows, peer_padding, valid_seq;
+  FastDiv div_heads, div_batch, div_seq;  // row -> (peer, seq, batch, head)
   int streams;
   const float* cos;
   const float* sin;
@@ -65,6 +69,18 @@ __device__ __forceinline__ void load_row8(const T* p, int valid, float (&out)[8]
   }
 }
 
+// Row index -> (peer, seq, batch, head) of the [peer, seq, batch, head] order.
+__device__ __forceinline__ void split_row(uint32_t r, FastDiv dh, FastDiv db, FastDiv ds,
+                                          uint32_t& peer, uint32_t& s, uint32_t& bat,
+                                          uint32_t& head) {
+  const uint32_t q1 = fast_div(r, dh);
+  head = r - q1 * dh.d;
+  const uint32_t q2 = fast_div(q1, db);
+  bat = q1 - q2 * db.d;
+  peer = fast_div(q2, ds);
+  s = q2 - peer * ds.d;
+}
+
 template <typename T, bool kVec>
 __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int group) {
   const int slot = blockIdx.y;
@@ -74,12 +90,10 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5)) *
                           rows_per_warp + lane / group;
   const bool live = row < a.rows;
-  const int64_t r = live ? row : 0;
-  const int64_t head = r % a.heads;
-  const int64_t bat = (r / a.heads) % a.batch;
-  const int64_t s = (r / (a.heads * a.batch)) % a.seq;
-  const int64_t peer = r / a.peer_rows;
-  const bool inside = peer * a.seq + s < a.valid_seq;
+  uint32_t peer, s, bat, head;
+  split_row(live ? static_cast<uint32_t>(row) : 0u, a.div_heads, a.div_batch, a.div_seq, peer, s,
+            bat, head);
+  const bool inside = static_cast<int64_t>(peer) * a.seq + s < a.valid_seq;
   const T* src = static_cast<const T*>(a.src[slot]);
   if (inside) src += peer * a.st[slot][0] + s * a.st[slot][1] + bat * a.st[slot][2] + head * a.st[slot][3];
   const int c0 = sub * 8;
@@ -91,18 +105,41 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
   if (inside && a.rotary > 0 && slot < 2 && c0 < a.rotary) {
     // Fused pre-A2A RoPE (h3_partial_rope.py:9-29): bf16 result, then encode.
     const int64_t half = a.rotary / 2;
-    float p[8];
+    const float* cs = a.cos + static_cast<int64_t>(s) * a.rotary;
+    const float* sn = a.sin + static_cast<int64_t>(s) * a.rotary;
+    float p[8], cv[8], sv[8];
+    if (kVec && valid == 8 && c0 + 8 <= a.rotary && half % 8 == 0 && a.rotary % 4 == 0) {
+      // The 8 channels sit on one side of the half split: the partner
+      // channels and the cos/sin entries are contiguous vectors.
+      const bool first = c0 < half;
+      load_row8<T, true>(src + (first ? c0 + half : c0 - half), 8, p);
+      const float4 c_lo = __ldg(reinterpret_cast<const float4*>(cs + c0));
+      const float4 c_hi = __ldg(reinterpret_cast<const float4*>(cs + c0 + 4));
+      const float4 s_lo = __ldg(reinterpret_cast<const float4*>(sn + c0));
+      const float4 s_hi = __ldg(reinterpret_cast<const float4*>(sn + c0 + 4));
+      cv[0] = c_lo.x; cv[1] = c_lo.y; cv[2] = c_lo.z; cv[3] = c_lo.w;
+      cv[4] = c_hi.x; cv[5] = c_hi.y; cv[6] = c_hi.z; cv[7] = c_hi.w;
+      sv[0] = s_lo.x; sv[1] = s_lo.y; sv[2] = s_lo.z; sv[3] = s_lo.w;
+      sv[4] = s_hi.x; sv[5] = s_hi.y; sv[6] = s_hi.z; sv[7] = s_hi.w;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t c = c0 + i;
-      if (i < valid && c < a.rotary) {
-        const bool first = c < half;
-        p[i] = to_f<T>(src[first ? c + half : c - half]);
-        const float cb = bf16_round(a.cos[s * a.rotary + c]);
-        const float sb = bf16_round(a.sin[s * a.rotary + c]);
-        const float left = bf16_round(__fmul_rn(x[i], cb));
-        const float right = bf16_round(__fmul_rn(first ? -p[i] : p[i], sb));
+      for (int i = 0; i < 8; ++i) {
+        const float left = bf16_round(__fmul_rn(x[i], bf16_round(cv[i])));
+        const float right = bf16_round(__fmul_rn(first ? -p[i] : p[i], bf16_round(sv[i])));
         x[i] = to_f<T>(from_f<T>(__fadd_rn(left, right)));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t c = c0 + i;
+        if (i < valid && c < a.rotary) {
+          const bool first = c < half;
+          p[i] = to_f<T>(src[first ? c + half : c - half]);
+          const float cb = bf16_round(cs[c]);
+          const float sb = bf16_round(sn[c]);
+          const float left = bf16_round(__fmul_rn(x[i], cb));
+          const float right = bf16_round(__fmul_rn(first ? -p[i] : p[i], sb));
+          x[i] = to_f<T>(from_f<T>(__fadd_rn(left, right)));
+        }
       }
     }
   }
@@ -113,26 +150,34 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
   const float scale = fmaxf(__fdiv_rn(m, 448.0f), 1.0e-12f);
   if (!live) return;
 
-  const int64_t wire_row = row + (peer * (a.streams - 1) + slot) * a.peer_rows;
-  const int64_t offset = wire_row * (a.width + 4) + peer * a.peer_padding;
+  const int64_t wire_row = row + (static_cast<int64_t>(peer) * (a.streams - 1) + slot) * a.peer_rows;
+  const int64_t offset = wire_row * (a.width + 4) + static_cast<int64_t>(peer) * a.peer_padding;
   uint8_t* dst = a.payload + offset;
-  uint8_t b[8];
+  // x / scale, correctly rounded as the reference's division, then e4m3.
+  const float y = __frcp_rn(scale);
+  uint32_t w[2];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float q = fminf(fmaxf(__fdiv_rn(x[i], scale), -448.0f), 448.0f);
-    b[i] = f32_to_e4m3(q);
+  for (int h = 0; h < 2; ++h) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float q = fminf(fmaxf(div_by(x[4 * h + j], scale, y), -448.0f), 448.0f);
+      word |= static_cast<uint32_t>(f32_to_e4m3(q)) << (8 * j);
+    }
+    w[h] = word;
   }
   if (valid == 8) {
     // Rows start at 4-byte multiples (width % 4 == 0), so two u32 stores.
-    reinterpret_cast<uint32_t*>(dst + c0)[0] = *reinterpret_cast<uint32_t*>(b);
-    reinterpret_cast<uint32_t*>(dst + c0)[1] = *reinterpret_cast<uint32_t*>(b + 4);
+    reinterpret_cast<uint32_t*>(dst + c0)[0] = w[0];
+    reinterpret_cast<uint32_t*>(dst + c0)[1] = w[1];
   } else {
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(w);
     for (int i = 0; i < valid; ++i) dst[c0 + i] = b[i];
   }
   if (sub == 0) *reinterpret_cast<float*>(dst + a.width) = scale;
   if (a.peer_padding && sub == 0 && slot == 0 && row % a.peer_rows == 0) {
     const int64_t packet = a.peer_rows * a.streams * (a.width + 4);
-    uint8_t* tail = a.payload + peer * (packet + a.peer_padding) + packet;
+    uint8_t* tail = a.payload + static_cast<int64_t>(peer) * (packet + a.peer_padding) + packet;
     for (int64_t i = 0; i < a.peer_padding; ++i) tail[i] = 0;
   }
 }
@@ -142,6 +187,7 @@ struct DecodeArgs {
   void* dst[kMaxStreams];
   int64_t st[kMaxStreams][4];  // element strides of the destination: peer, seq, batch, head
   int64_t seq, batch, heads, width, rows, peer_rows, peer_padding, valid_seq;
+  FastDiv div_heads, div_batch, div_seq;
   int streams;
 };
 
@@ -157,11 +203,9 @@ __global__ void __launch_bounds__(kThreads) wire_decode_kernel(DecodeArgs a, int
   const int c0 = sub * 8;
   const int valid = max(0, min(8, static_cast<int>(a.width) - c0));
   if (valid == 0) return;
-  const int64_t peer = row / a.peer_rows;
-  const int64_t head = row % a.heads;
-  const int64_t bat = (row / a.heads) % a.batch;
-  const int64_t s = (row / (a.heads * a.batch)) % a.seq;
-  if (peer * a.seq + s >= a.valid_seq) return;
+  uint32_t peer, s, bat, head;
+  split_row(static_cast<uint32_t>(row), a.div_heads, a.div_batch, a.div_seq, peer, s, bat, head);
+  if (static_cast<int64_t>(peer) * a.seq + s >= a.valid_seq) return;
   const int64_t wire_row = row + (peer * (a.streams - 1) + slot) * a.peer_rows;
   const uint8_t* src = a.payload + wire_row * (a.width + 4) + peer * a.peer_padding;
   const float scale = __ldg(reinterpret_cast<const float*>(src + a.width));
@@ -224,9 +268,13 @@ XGB_API int xgb_fp8_wire_encode_view(const void* const* sources, const int64_t* 
     if (reinterpret_cast<uintptr_t>(sources[s]) & 15u) vec = false;
   }
   if (width % 8) vec = false;
+  if (a.rows > INT32_MAX) return XGB_ERR_SHAPE;
   a.peers = peers; a.seq = seq; a.batch = batch; a.heads = heads; a.width = width;
   a.peer_rows = a.rows / peers;
   a.peer_padding = peer_padding; a.streams = streams; a.valid_seq = valid_seq;
+  a.div_heads = make_fastdiv(static_cast<uint32_t>(heads));
+  a.div_batch = make_fastdiv(static_cast<uint32_t>(batch));
+  a.div_seq = make_fastdiv(static_cast<uint32_t>(seq));
   a.cos = cos; a.sin = sin; a.rotary = rotary; a.payload = payload;
   const int group = group_for(width);
   const int64_t rows_per_block = (kThreads / 32) * (32 / group);
@@ -274,9 +322,13 @@ XGB_API int xgb_fp8_wire_decode_view(const uint8_t* payload, void* const* dests,
     a.dst[s] = dests[s];
     for (int d = 0; d < 4; ++d) a.st[s][d] = strides[4 * s + d];
   }
+  if (a.rows > INT32_MAX) return XGB_ERR_SHAPE;
   a.seq = seq; a.batch = batch; a.heads = heads; a.width = width;
   a.peer_rows = a.rows / peers;
   a.peer_padding = peer_padding; a.streams = streams; a.valid_seq = valid_seq;
+  a.div_heads = make_fastdiv(static_cast<uint32_t>(heads));
+  a.div_batch = make_fastdiv(static_cast<uint32_t>(batch));
+  a.div_seq = make_fastdiv(static_cast<uint32_t>(seq));
   const int group = group_for(width);
   const int64_t rows_per_block = (kThreads / 32) * (32 / group);
   dim3 grid(static_cast<unsigned>(cdiv(a.rows, rows_per_block)), streams);

@@ -66,16 +66,6 @@ __device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
   for (int j = 0; j < 8; ++j) x[j] = tf<T>(e[j]);
 }
 
-// a / b correctly rounded, for a divisor shared by many quotients: with
-// y = RN(1/b), q = RN(a*y) and the exact remainder r = a - b*q (one FMA),
-// RN(q + r*y) is the correctly rounded quotient (Markstein's correction,
-// P. Markstein, IBM J. Res. Dev. 34(1), 1990) for normal b and quotient.
-__device__ __forceinline__ float div_by(float a, float b, float y) {
-  const float q = __fmul_rn(a, y);
-  const float r = __fmaf_rn(-q, b, a);
-  return __fmaf_rn(r, y, q);
-}
-
 // Per 512-row chunk of one head: channel sums of K and channel abs-max of V.
 // Thread t owns channels 8*(t%16)..+8 of rows t/16 + 16*i (16-byte loads).
 template <typename T>

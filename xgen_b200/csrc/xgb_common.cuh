@@ -43,6 +43,36 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
   return __half2float(__half(h));
 }
 
+// Unsigned division by a divisor fixed for a whole launch, as a multiply-high
+// and shifts (T. Granlund, P. Montgomery, "Division by Invariant Integers
+// using Multiplication", PLDI 1994): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (t + ((n - t) >> 1)) >> (l - 1)
+// where t = mulhi(n, m), for every 32-bit n (d = 1 is special-cased).
+struct FastDiv {
+  uint32_t d, m, l;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while (l < 32 && (uint64_t{1} << l) < d) ++l;
+  const uint64_t m = ((uint64_t{1} << 32) * ((uint64_t{1} << l) - d)) / d + 1;
+  return FastDiv{d, static_cast<uint32_t>(m), l};
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) {
+  if (f.l == 0) return n;
+  const uint32_t t = __umulhi(n, f.m);
+  return (t + ((n - t) >> 1)) >> (f.l - 1);
+}
+
+// a / b correctly rounded for a divisor shared by many quotients: with
+// y = RN(1/b), q = RN(a*y) and the exact remainder r = a - b*q (one FMA),
+// RN(q + r*y) is the correctly rounded quotient (Markstein's correction,
+// P. Markstein, IBM J. Res. Dev. 34(1), 1990) for normal b and quotient.
+__device__ __forceinline__ float div_by(float a, float b, float y) {
+  const float q = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q, b, a);
+  return __fmaf_rn(r, y, q);
+}
+
 // Block-wide reduction helpers (warp shuffles, then one shared slot per warp).
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
