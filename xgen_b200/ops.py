@@ -170,11 +170,17 @@ def norm_modulate_quant(x: torch.Tensor, norm: str, weight, eps: float, scale: t
 
 def output_adaln(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
                  indices: torch.Tensor, *, norm: str = "layernorm", weight=None,
-                 eps: float = 1e-6) -> torch.Tensor:
-    """Final-layer output AdaLN of the H3 transformer (`norm_out`:
+                 eps: float = 1e-6, fused: bool = False) -> torch.Tensor:
+    """Final-layer output AdaLN of the H3 transformer (`norm_out`,
     x_diffusers/x_diffusers/framework/transformer/minimax_h3.py:672-696):
-    bf16(bf16(norm(x) * bf16(1 + scale[idx])) + shift[idx]) in one pass;
-    scale/shift are the [M, H] tables of lookup_final()."""
+    bf16(bf16(norm(x) * bf16(1 + scale[idx])) + shift[idx]); scale/shift are
+    the [M, H] tables of lookup_final().
+
+    Default: the reference's own LayerNorm followed by the bit-exact
+    indexed-affine kernel, bitwise equal to the reference's fused output path
+    (x_base/tests/test_h3_output_adaln.py:29-45). fused=True runs norm and
+    modulation in one pass (xgb_norm_modulate_quant without the e4m3
+    output), whose fp32 statistics can round a value one bf16 ulp apart."""
     _require_cuda(x, scale, shift, indices, what="H3 output AdaLN")
     if (x.ndim != 3 or x.dtype != torch.bfloat16 or x.stride(-1) != 1 or x.stride(0) != x.shape[1] * x.stride(1)
             or scale.dtype != torch.bfloat16 or shift.dtype != torch.bfloat16
@@ -182,6 +188,12 @@ def output_adaln(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
             or indices.numel() != x.shape[1] or norm not in ("layernorm", "rmsnorm")):
         raise ValueError("output_adaln needs bf16 [B,S,H] rows, bf16 tables, int64 [S] indices")
     b, s, h = x.shape
+    if not fused:
+        if norm == "layernorm":
+            n = torch.nn.functional.layer_norm(x, (h,), eps=eps)
+        else:
+            n = torch.nn.functional.rms_norm(x, (h,), weight, eps=eps)
+        return indexed_affine(n, scale, shift, indices, modulation=True)
     out = torch.empty((b, s, h), device=x.device, dtype=torch.bfloat16)
     call("xgb_norm_modulate_quant", x.data_ptr(), x.stride(1), b * s, h, s,
          1 if norm == "rmsnorm" else 0, weight.data_ptr() if weight is not None else None,
