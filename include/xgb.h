@@ -170,6 +170,19 @@ int xgb_fp8_quantize_per_tensor(const void* x, int dtype, int64_t n, uint8_t* ou
 int xgb_fp8_quantize_per_tensor_noalloc(const void* x, int dtype, int64_t n, uint8_t* out,
                                         float* scale_out, void* stream);
 
+/* The two halves of xgb_fp8_quantize_per_tensor, for a scale shared by a
+ * process group: xgb_fp8_abs_peak_scale writes scale_out = max(amax/448,
+ * FLT_MIN) (workspace as for xgb_fp8_quantize_per_tensor); the caller may
+ * then all-reduce it with MAX; xgb_fp8_quantize_with_scale writes
+ * out = e4m3(clamp(x/scale, +-448)) with the device scalar *scale.
+ * Replace quantize_activation(x, group=...),
+ * x_base/x_base/operator/h3_fp8_quant.py:18-25 (used by H3FP8TPLinear,
+ * h3_fp8.py:58-68). */
+int xgb_fp8_abs_peak_scale(const void* x, int dtype, int64_t n, float* scale_out, void* workspace,
+                           int64_t workspace_bytes, void* stream);
+int xgb_fp8_quantize_with_scale(const void* x, int dtype, int64_t n, const float* scale,
+                                uint8_t* out, void* stream);
+
 /* Per-token dynamic e4m3 (the per-token scaling of the B200 FP8 Linear):
  * scales[r] = max(amax(|x[r,:]|)/448, FLT_MIN), out[r,c] = e4m3(x/scale).
  * x rows strided by row_stride elements; out contiguous [rows, cols].

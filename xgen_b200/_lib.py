@@ -51,6 +51,8 @@ SIGNATURES = {
                                          c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_vp]),
     "xgb_fp8_quantize_per_tensor_workspace": (c_i64, [c_i64]),
     "xgb_fp8_quantize_per_tensor": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "xgb_fp8_abs_peak_scale": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_i64, c_vp]),
+    "xgb_fp8_quantize_with_scale": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp]),
     "xgb_fp8_quantize_per_tensor_noalloc": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp]),
     "xgb_fp8_quantize_per_token": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "xgb_fp8_gemm": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_int,

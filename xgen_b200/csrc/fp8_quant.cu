@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(const T* __restrict__ x,
                                                         const float* __restrict__ scale_ptr,
                                                         uint8_t* __restrict__ out) {
   const float scale = __ldg(scale_ptr);
+  const float y = __frcp_rn(scale);
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 8;
   if (i >= n) return;
   if (i + 8 <= n && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
@@ -96,11 +97,11 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(const T* __restrict__ x,
     uint8_t b[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      b[j] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(v[j]), scale), -448.f), 448.f));
+      b[j] = f32_to_e4m3(fminf(fmaxf(div_by(to_float<T>(v[j]), scale, y), -448.f), 448.f));
     *reinterpret_cast<uint2*>(out + i) = *reinterpret_cast<uint2*>(b);
   } else {
     for (int64_t j = i; j < min(i + 8, n); ++j)
-      out[j] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(x[j]), scale), -448.f), 448.f));
+      out[j] = f32_to_e4m3(fminf(fmaxf(div_by(to_float<T>(x[j]), scale, y), -448.f), 448.f));
   }
 }
 
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(kThreads) per_token_kernel(const T* __restrict
   const float amax_scale = __fdiv_rn(__int_as_float(m), 448.0f);
   const float scale = isnan(amax_scale) ? amax_scale : fmaxf(amax_scale, FLT_MIN);
   if (lane == 0) scales[row] = scale;
+  const float y = __frcp_rn(scale);
   if (vec) {
     for (int64_t c = lane * 8; c < cols; c += 256) {
       uint4 raw = __ldg(reinterpret_cast<const uint4*>(src + c));
@@ -140,12 +142,12 @@ __global__ void __launch_bounds__(kThreads) per_token_kernel(const T* __restrict
       uint8_t b[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        b[j] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(v[j]), scale), -448.f), 448.f));
+        b[j] = f32_to_e4m3(fminf(fmaxf(div_by(to_float<T>(v[j]), scale, y), -448.f), 448.f));
       *reinterpret_cast<uint2*>(dst + c) = *reinterpret_cast<uint2*>(b);
     }
   } else {
     for (int64_t c = lane; c < cols; c += 32)
-      dst[c] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(to_float<T>(src[c]), scale), -448.f), 448.f));
+      dst[c] = f32_to_e4m3(fminf(fmaxf(div_by(to_float<T>(src[c]), scale, y), -448.f), 448.f));
   }
 }
 
@@ -182,6 +184,40 @@ XGB_API int xgb_fp8_quantize_per_tensor(const void* x, int dtype, int64_t n, uin
     peak_to_scale_kernel<<<1, kThreads, 0, st>>>(peaks, blocks, scale_out);
     pack_kernel<<<pack_grid, kThreads, 0, st>>>(xh, n, scale_out, out);
   }
+  return launch_status();
+}
+
+XGB_API int xgb_fp8_abs_peak_scale(const void* x, int dtype, int64_t n, float* scale_out,
+                                   void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!x || !scale_out) return XGB_ERR_ARG;
+  if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
+  if (n <= 0) return XGB_ERR_SHAPE;
+  const int64_t blocks = cdiv(n, kPeakBlock);
+  if (!workspace || workspace_bytes < xgb_fp8_quantize_per_tensor_workspace(n))
+    return XGB_ERR_WORKSPACE;
+  int* peaks = static_cast<int*>(workspace);
+  cudaStream_t st = as_stream(stream);
+  if (dtype == XGB_BF16)
+    abs_peak_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), n, peaks);
+  else
+    abs_peak_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+        static_cast<const __half*>(x), n, peaks);
+  peak_to_scale_kernel<<<1, kThreads, 0, st>>>(peaks, blocks, scale_out);
+  return launch_status();
+}
+
+XGB_API int xgb_fp8_quantize_with_scale(const void* x, int dtype, int64_t n, const float* scale,
+                                        uint8_t* out, void* stream) {
+  if (!x || !out || !scale) return XGB_ERR_ARG;
+  if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
+  if (n <= 0) return XGB_ERR_SHAPE;
+  cudaStream_t st = as_stream(stream);
+  const unsigned grid = static_cast<unsigned>(cdiv(cdiv(n, 8), kThreads));
+  if (dtype == XGB_BF16)
+    pack_kernel<<<grid, kThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, scale, out);
+  else
+    pack_kernel<<<grid, kThreads, 0, st>>>(static_cast<const __half*>(x), n, scale, out);
   return launch_status();
 }
 

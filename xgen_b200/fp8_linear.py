@@ -112,7 +112,7 @@ class H3FP8Linear(nn.Module):
 
     def _quantize(self, matrix):
         if self.scaling == "per_tensor":
-            q, s = quantize_activation(matrix)
+            q, s = quantize_activation(matrix, group=getattr(self, "activation_group", None))
             return q, s.reshape(1), 0
         q, s = quantize_per_token(matrix)
         return q, s, 1
@@ -184,3 +184,54 @@ class H3FP8Linear(nn.Module):
              torch.cuda.current_stream(device).cuda_stream)
         self.calls += 1
         return out.reshape(out_shape)
+
+
+class H3FP8TPLinear(H3FP8Linear):
+    """H3FP8Linear inside tensor parallelism, keeping the column/row
+    communication of the layer it replaces (x_base/x_base/operator/h3_fp8.py
+    :71-108): column-parallel layers apply their bias locally and optionally
+    all-gather the output; row-parallel layers take (or slice) their input
+    shard, all-reduce the partial products (or call `reduce_fn`) and add the
+    bias after the reduction. Set `activation_group` to share one activation
+    scale across the group (MAX all-reduce before packing).
+
+    `original` carries weight/bias and the TP attributes `column_parallel`
+    (or is an instance named ColumnParallelLinear), `gather_output`,
+    `input_is_parallel`, `tp_group`, `reduce_fn`."""
+
+    def __init__(self, original, scaling: str = "per_tensor"):
+        bias = getattr(original, "bias", None)
+        super().__init__(original.weight, bias, scaling=scaling)
+        column = getattr(original, "column_parallel", None)
+        self.column_parallel = (type(original).__name__ == "ColumnParallelLinear"
+                                if column is None else bool(column))
+        self.gather_output = getattr(original, "gather_output", False)
+        self.input_is_parallel = getattr(original, "input_is_parallel", True)
+        self.tp_group = getattr(original, "tp_group", None)
+        self.reduce_fn = getattr(original, "reduce_fn", None)
+
+    def forward(self, x):
+        import torch.distributed as dist
+
+        group = self.tp_group
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if not self.column_parallel and not self.input_is_parallel and world > 1:
+            x = x.chunk(world, dim=-1)[dist.get_rank(group)]
+        bias = self.bias
+        if not self.column_parallel:
+            self.bias = None  # row bias belongs after the reduction
+        try:
+            output = self._forward(x, None)
+        finally:
+            self.bias = bias
+        if world > 1:
+            if self.column_parallel and self.gather_output:
+                values = [torch.empty_like(output) for _ in range(world)]
+                dist.all_gather(values, output, group=group)
+                output = torch.cat(values, dim=-1)
+            elif not self.column_parallel:
+                if self.reduce_fn is None:
+                    dist.all_reduce(output, group=group)
+                else:
+                    output = self.reduce_fn(output, group)
+        return output + bias if not self.column_parallel and bias is not None else output

@@ -122,10 +122,12 @@ def gate_first_swiglu(x: torch.Tensor, *, with_amax: bool = False):
     return (out, amax) if with_amax else out
 
 
-def quantize_activation(x: torch.Tensor):
+def quantize_activation(x: torch.Tensor, group=None):
     """Per-tensor dynamic e4m3 (scale = max(amax/448, FLT_MIN)); bit-exact
     with quantize_activation / quantize_per_tensor of
-    x_base/x_base/operator/h3_fp8_quant.py:18-25 and h3_fp8.py:9-12."""
+    x_base/x_base/operator/h3_fp8_quant.py:18-25 and h3_fp8.py:9-12. With a
+    process group the scale is all-reduced with MAX before packing, so every
+    rank of a tensor-parallel group packs with the same scale."""
     _require_cuda(x, what="H3 FP8 quantization")
     if x.dtype not in _DTYPE_CODE:
         raise ValueError("H3 FP8 quantization requires a bf16/fp16 tensor")
@@ -135,11 +137,24 @@ def quantize_activation(x: torch.Tensor):
     n = x.numel()
     if n == 0:
         scale.fill_(torch.finfo(torch.float32).tiny)
+        if group is not None:
+            import torch.distributed as dist
+
+            dist.all_reduce(scale, op=dist.ReduceOp.MAX, group=group)
         return out, scale
     ws_bytes = _lib.lib().xgb_fp8_quantize_per_tensor_workspace(n)
     ws = torch.empty(max(ws_bytes, 4), device=x.device, dtype=torch.uint8)
-    call("xgb_fp8_quantize_per_tensor", x.data_ptr(), _DTYPE_CODE[x.dtype], n, out.data_ptr(),
-         scale.data_ptr(), ws.data_ptr(), ws_bytes, _stream(x))
+    if group is None:
+        call("xgb_fp8_quantize_per_tensor", x.data_ptr(), _DTYPE_CODE[x.dtype], n, out.data_ptr(),
+             scale.data_ptr(), ws.data_ptr(), ws_bytes, _stream(x))
+        return out, scale
+    import torch.distributed as dist
+
+    call("xgb_fp8_abs_peak_scale", x.data_ptr(), _DTYPE_CODE[x.dtype], n, scale.data_ptr(),
+         ws.data_ptr(), ws_bytes, _stream(x))
+    dist.all_reduce(scale, op=dist.ReduceOp.MAX, group=group)
+    call("xgb_fp8_quantize_with_scale", x.data_ptr(), _DTYPE_CODE[x.dtype], n, scale.data_ptr(),
+         out.data_ptr(), _stream(x))
     return out, scale
 
 
