@@ -270,7 +270,17 @@ int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void* k,
 int xgb_attention_sage(const int8_t* q8, const float* q_scale, const int8_t* k8,
                        const float* k_scale, const uint8_t* v8, const float* v_scale,
                        int64_t batch, int64_t heads, int64_t seq, void* out,
-                       const int64_t* out_strides, int* error_flag, void* stream);
+                       const int64_t* out_strides, void* split_workspace,
+                       int64_t split_workspace_bytes, int* error_flag, void* stream);
+
+/* Both attention entry points take an optional tail-split workspace
+ * (xgb_attention_split_workspace_bytes() bytes, zeroed once by the caller;
+ * NULL or smaller disables the split). A launch runs one CTA per (batch*
+ * head, 256 query rows), one CTA per SM; the items of the last, partial
+ * wave are split along the key range across the idle SMs and merged by the
+ * last part to finish, so that wave costs a fraction of a full one. The
+ * workspace is used stream-ordered: launches that share it must not overlap. */
+int64_t xgb_attention_split_workspace_bytes(void);
 
 /* Non-causal BF16 attention (tcgen05 kind::f16, fp32 accumulation) reading
  * q [b, h, seq_q, 128] and k/v [b, h, seq_kv, 128] views in place through
@@ -280,7 +290,8 @@ int xgb_attention_sage(const int8_t* q8, const float* q_scale, const int8_t* k8,
 int xgb_attention_bf16(const void* q, const int64_t* q_strides, const void* k,
                        const int64_t* k_strides, const void* v, const int64_t* v_strides,
                        int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_kv,
-                       float sm_scale, void* out, const int64_t* out_strides, int* error_flag,
+                       float sm_scale, void* out, const int64_t* out_strides,
+                       void* split_workspace, int64_t split_workspace_bytes, int* error_flag,
                        void* stream);
 
 #ifdef __cplusplus

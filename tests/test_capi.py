@@ -56,7 +56,7 @@ def test_argument_errors_without_gpu():
     assert h.xgb_fp8_quantize_per_tensor_workspace(8193) == 8
     strides = _lib.i64_array([0, 0, 0, 1])
     assert h.xgb_attention_sage(dummy, dummy, dummy, dummy, dummy, dummy, 1, 1, 0, dummy, strides,
-                                None, None) == -2
+                                None, 0, None, None) == -2
 
 
 def test_ops_refuse_cpu_tensors():

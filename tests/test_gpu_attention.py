@@ -108,3 +108,49 @@ def test_backend_contract(cuda_device):
         masked = backend(q, k, v, attn_mask=mask)
         assert backend.calls == 2 and backend.kernel_calls == 1
         assert masked.shape == q.shape
+
+
+@pytest.mark.parametrize("precision", ["bf16", "sage"])
+@pytest.mark.parametrize("h,s", [(1, 20000), (3, 4097), (5, 9001)])
+def test_tail_split_matches_unsplit(cuda_device, precision, h, s):
+    """The last partial wave's items split along the key range (merged by the
+    last part to finish) give the unsplit result up to fp32 summation order
+    (BF16) or to the e4m3 rounding of P, which each part takes against its own
+    running max (Sage, the Sage parity bar); the workspace stays reusable
+    (counters reset) and the result deterministic across launches. The
+    small-shape oracle tests above run split (fewer items than SMs)."""
+    from xgen_b200 import attention as A
+    from xgen_b200._lib import call, i64_array
+
+    g = torch.Generator().manual_seed(h * s)
+    q, k, v = (torch.randn(1, h, s, 128, generator=g).bfloat16().to(cuda_device) for _ in range(3))
+    ws = A.SageWorkspace(1, h, s, cuda_device) if precision == "sage" else None
+    if ws is not None:
+        A.sage_prepare(q, k, v, ws=ws)
+
+    def run(split: bool):
+        out = torch.empty_like(q)
+        wsp, wsb = A._ws_args(cuda_device) if split else (None, 0)
+        if precision == "sage":
+            call("xgb_attention_sage", ws.q8.data_ptr(), ws.q_scale.data_ptr(), ws.k8.data_ptr(),
+                 ws.k_scale.data_ptr(), ws.v8.data_ptr(), ws.v_scale.data_ptr(), 1, h, s,
+                 out.data_ptr(), i64_array(out.stride()), wsp, wsb,
+                 A._err_flag(cuda_device).data_ptr(), A._stream(out))
+        else:
+            call("xgb_attention_bf16", q.data_ptr(), i64_array(q.stride()), k.data_ptr(),
+                 i64_array(k.stride()), v.data_ptr(), i64_array(v.stride()), 1, h, s, s,
+                 128 ** -0.5, out.data_ptr(), i64_array(out.stride()), wsp, wsb,
+                 A._err_flag(cuda_device).data_ptr(), A._stream(out))
+        return out
+
+    whole = run(False)
+    parts = [run(True) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert A.kernel_errors() == 0
+    a = whole.float().cpu().numpy()
+    tol = (0.99999, 1e-2) if precision == "bf16" else (0.999, 5e-2)
+    for p in parts:
+        b = p.float().cpu().numpy()
+        assert oa.cosine(a, b) >= tol[0]
+        assert np.abs(a - b).max() <= tol[1]
+    assert torch.equal(parts[0], parts[1]) and torch.equal(parts[1], parts[2])

@@ -63,10 +63,11 @@ SIGNATURES = {
     "xgb_sage_prepare": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_int, c_i64, c_i64,
                                  c_i64, c_i64, c_float, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                  c_i64, c_vp]),
+    "xgb_attention_split_workspace_bytes": (c_i64, []),
     "xgb_attention_sage": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
-                                   c_i64p, c_vp, c_vp]),
+                                   c_i64p, c_vp, c_i64, c_vp, c_vp]),
     "xgb_attention_bf16": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_i64, c_i64, c_i64,
-                                   c_i64, c_float, c_vp, c_i64p, c_vp, c_vp]),
+                                   c_i64, c_float, c_vp, c_i64p, c_vp, c_i64, c_vp, c_vp]),
 }
 
 _lock = threading.Lock()

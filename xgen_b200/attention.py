@@ -33,11 +33,32 @@ def _err_flag(device: torch.device) -> torch.Tensor:
     return flag
 
 
+_split_workspaces: dict[int, torch.Tensor] = {}
+
+
+def _split_ws(device: torch.device) -> torch.Tensor:
+    """Per-device workspace for the attention kernels' tail split (zeroed
+    once; the kernels leave it reusable; launches on one device are
+    stream-ordered through the caller's stream)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _split_workspaces.get(idx)
+    if ws is None:
+        ws = torch.zeros(_lib.lib().xgb_attention_split_workspace_bytes(), dtype=torch.uint8,
+                         device=device)
+        _split_workspaces[idx] = ws
+    return ws
+
+
 def kernel_errors(device: torch.device | None = None) -> int:
     """Non-zero if a tcgen05 kernel on `device` gave up on a bounded wait
     (synchronises the device)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     return int(_err_flag(device).item())
+
+
+def _ws_args(device: torch.device):
+    ws = _split_ws(device)
+    return ws.data_ptr(), ws.numel()
 
 
 def _stream(t: torch.Tensor) -> int:
@@ -103,7 +124,8 @@ def sage_attention_prepared(ws: SageWorkspace, out: torch.Tensor | None = None) 
         raise ValueError("Sage attention output must be a bf16 [B, H, S, 128] view")
     call("xgb_attention_sage", ws.q8.data_ptr(), ws.q_scale.data_ptr(), ws.k8.data_ptr(),
          ws.k_scale.data_ptr(), ws.v8.data_ptr(), ws.v_scale.data_ptr(), b, h, s, out.data_ptr(),
-         i64_array(out.stride()), _err_flag(out.device).data_ptr(), _stream(out))
+         i64_array(out.stride()), *_ws_args(out.device), _err_flag(out.device).data_ptr(),
+         _stream(out))
     return out
 
 
@@ -127,7 +149,8 @@ def dense_attention(q, k, v, sm_scale: float | None = None, out=None) -> torch.T
         out = torch.empty((b, h, sq, d), dtype=torch.bfloat16, device=q.device)
     call("xgb_attention_bf16", q.data_ptr(), i64_array(q.stride()), k.data_ptr(),
          i64_array(k.stride()), v.data_ptr(), i64_array(v.stride()), b, h, sq, skv, sm_scale,
-         out.data_ptr(), i64_array(out.stride()), _err_flag(q.device).data_ptr(), _stream(q))
+         out.data_ptr(), i64_array(out.stride()), *_ws_args(q.device), _err_flag(q.device).data_ptr(),
+         _stream(q))
     return out
 
 

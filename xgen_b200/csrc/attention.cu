@@ -72,6 +72,7 @@ __device__ __forceinline__ bool poly_pair(int pair) {
 #endif
 constexpr bool kTurn = XGB_ATTN_TURN != 0;
 constexpr int kTurnBar = 1;  // named barriers 1, 2: exp turn of WG0, WG1
+constexpr int kEpiBar = 3;   // named barrier 3: the 256 softmax threads in the split epilogue
 constexpr uint32_t kMagic = 0x4B400000u;
 
 template <bool kSage>
@@ -109,6 +110,17 @@ struct Params {
   __nv_bfloat16* out;
   int64_t osb, osh, oss;
   int* err;
+  // Tail balancing. CTAs [0, n_full) each run one work item, a (batch*head,
+  // Q-tile pair); CTA n_full + j runs part j % splits of the KV range of item
+  // n_full + j / splits and leaves its unnormalised O and (max, sum) rows in
+  // part_o / part_ml; the last part of an item to finish (counters) merges
+  // them. splits = 1: no split.
+  int n_qt;        // Q-tile pairs per (batch, head)
+  int n_full;
+  int splits;
+  float* part_o;   // [tail CTAs][256][128]
+  float* part_ml;  // [tail CTAs][256][2]
+  int* counters;   // [tail items], zero at launch
 };
 
 struct Barriers {
@@ -122,6 +134,7 @@ struct Barriers {
   uint64_t o_done[2];  // every P.V of Q tile i has landed in O_i
   uint64_t end[2];
   uint32_t tmem_base;
+  int last;  // this CTA finished the last part of its item (split epilogue)
 };
 
 // TMEM column of S/P buffer `b` of Q tile `i`, and of O_i.
@@ -170,9 +183,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   Barriers* bars = reinterpret_cast<Barriers*>(smem + C::kBarOff);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int m0 = blockIdx.x * (kQT * kBM);
-  const int n_kv = (p.seq_kv + kBN - 1) / kBN;
+  const int cta = blockIdx.x;
+  const bool split = cta >= p.n_full;
+  const int item = split ? p.n_full + (cta - p.n_full) / p.splits : cta;
+  const int bh = item / p.n_qt;
+  const int m0 = (item % p.n_qt) * (kQT * kBM);
+  // KV tiles [kv0, kv0 + n_kv) of this CTA; the host keeps every part non-empty.
+  const int n_all = (p.seq_kv + kBN - 1) / kBN;
+  const int per = split ? (n_all + p.splits - 1) / p.splits : n_all;
+  const int kv0 = split ? ((cta - p.n_full) % p.splits) * per : 0;
+  const int n_kv = split ? min(per, n_all - kv0) : n_all;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -218,11 +238,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t >= C::kStages) ok = mbar_wait(&bars->kv_empty[s], ((t / C::kStages) - 1) & 1, p.err);
         if (!ok) break;
         mbar_arrive_expect_tx(&bars->k_full[s], C::kKVBytes);
-        load_rows<kSage>(&k_map, smem + C::kKOff + s * C::kKVBytes, &bars->k_full[s], t * kBN, bh,
-                         p.heads, C::kSub);
+        load_rows<kSage>(&k_map, smem + C::kKOff + s * C::kKVBytes, &bars->k_full[s], (kv0 + t) * kBN,
+                         bh, p.heads, C::kSub);
         mbar_arrive_expect_tx(&bars->v_full[s], C::kKVBytes);
-        load_rows<kSage>(&v_map, smem + C::kVOff + s * C::kKVBytes, &bars->v_full[s], t * kBN, bh,
-                         p.heads, C::kSub);
+        load_rows<kSage>(&v_map, smem + C::kVOff + s * C::kKVBytes, &bars->v_full[s], (kv0 + t) * kBN,
+                         bh, p.heads, C::kSub);
         issued = t + 1;
       }
       // Never leave with copies in flight: wait (bounded) for the last ones.
@@ -298,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_used = kNegInf;
     float l = 0.f;
     float ks = 0.f;  // K-block scale of the current tile (Sage)
-    if constexpr (kSage) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride];
+    if constexpr (kSage) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0];
     bool ok = true;
     // The two warpgroups take turns in the MUFU-bound exp section so one's
     // exp overlaps the other's load/max/rescale work. The turn passes through
@@ -326,10 +346,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 127), a monotone map, so the max runs on floats and no conversion
       // instruction is needed. Padding keys (>= valid, last tile only) get a
       // sentinel far below any real score.
-      const int valid = p.seq_kv - t * kBN;
+      const int valid = p.seq_kv - (kv0 + t) * kBN;
       const float comb = kSage ? qs * ks : p.scale_log2;
       if constexpr (kSage) {
-        if (t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + t + 1];
+        if (t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0 + t + 1];
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -449,31 +469,97 @@ __global__ void __launch_bounds__(kThreads, 1)
     // pv_done may trail the last tile by two phases here, so a parity wait
     // on it would be ambiguous; o_done completes exactly once.
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[i], 0, p.err));
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-      const int b = bh / p.heads, h = bh % p.heads;
-      __nv_bfloat16* dst = p.out + b * p.osb + h * p.osh + static_cast<int64_t>(row) * p.oss;
+    const int b = bh / p.heads, h = bh % p.heads;
+    __nv_bfloat16* dst = p.out + b * p.osb + h * p.osh + static_cast<int64_t>(row) * p.oss;
+    const float* vsc = kSage ? p.v_scale + static_cast<int64_t>(bh) * kD : nullptr;
+    // out row = o / l (times the per-channel V scale for Sage), as bf16.
+    auto store_row = [&](int c, const float* o, float inv_l) {
+      uint32_t w[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float x0 = o[e] * inv_l;
+        float x1 = o[e + 1] * inv_l;
+        if constexpr (kSage) {  // l sums the same kPScale-scaled P
+          x0 *= vsc[c * 32 + e];
+          x1 *= vsc[c * 32 + e + 1];
+        }
+        w[e / 2] = pack_bf16x2(x0, x1);
+      }
+      uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+    };
+    if (!split) {
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = l > 0.f ? 1.0f / l : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + c * 32, o);
-        tmem_ld_wait();
-        if (row < p.seq_q) {
-          uint32_t w[16];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_ld_wait();
+          if (row < p.seq_q) store_row(c, reinterpret_cast<const float*>(o), inv_l);
+        }
+      }
+    } else {
+      // Leave this part's rows, then the last part of the item merges:
+      // M = max m_q, O = sum 2^(m_q - M) O_q, L = sum 2^(m_q - M) l_q.
+      const int slot = cta - p.n_full;
+      const int first = slot - slot % p.splits;
+      const int r = i * kBM + lane_base + lane;  // row within the CTA
+      if (ok) {
+        tc_fence_after();
+        float4* po = reinterpret_cast<float4*>(p.part_o + (static_cast<int64_t>(slot) * 256 + r) * kD);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float x0 = __uint_as_float(o[e]) * inv_l;
-            float x1 = __uint_as_float(o[e + 1]) * inv_l;
-            if constexpr (kSage) {  // l sums the same kPScale-scaled P
-              x0 *= p.v_scale[static_cast<int64_t>(bh) * kD + c * 32 + e];
-              x1 *= p.v_scale[static_cast<int64_t>(bh) * kD + c * 32 + e + 1];
+          for (int v = 0; v < 8; ++v)
+            po[c * 8 + v] = make_float4(__uint_as_float(o[4 * v]), __uint_as_float(o[4 * v + 1]),
+                                        __uint_as_float(o[4 * v + 2]), __uint_as_float(o[4 * v + 3]));
+        }
+        reinterpret_cast<float2*>(p.part_ml)[static_cast<int64_t>(slot) * 256 + r] = make_float2(m_used, l);
+      }
+      __threadfence();
+      named_sync(kEpiBar, 2 * kBM);
+      if (threadIdx.x == 0) {
+        const int done = atomicAdd(&p.counters[slot / p.splits], 1);
+        bars->last = done == p.splits - 1;
+        if (bars->last) p.counters[slot / p.splits] = 0;  // ready for the next launch
+      }
+      named_sync(kEpiBar, 2 * kBM);
+      if (bars->last && ok && row < p.seq_q) {
+        __threadfence();
+        const float2* ml = reinterpret_cast<const float2*>(p.part_ml);
+        float mx = kNegInf;
+        for (int q = 0; q < p.splits; ++q) mx = fmaxf(mx, __ldcg(&ml[static_cast<int64_t>(first + q) * 256 + r]).x);
+        float lsum = 0.f;
+        for (int q = 0; q < p.splits; ++q) {
+          const float2 v = __ldcg(&ml[static_cast<int64_t>(first + q) * 256 + r]);
+          lsum += ex2_approx(v.x - mx) * v.y;
+        }
+        const float inv_l = lsum > 0.f ? 1.0f / lsum : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float acc[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+          for (int q = 0; q < p.splits; ++q) {
+            const int64_t base = static_cast<int64_t>(first + q) * 256 + r;
+            const float w = ex2_approx(__ldcg(&ml[base]).x - mx);
+            const float4* po = reinterpret_cast<const float4*>(p.part_o + base * kD) + c * 8;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const float4 o4 = __ldcg(po + v);
+              acc[4 * v] = fmaf(w, o4.x, acc[4 * v]);
+              acc[4 * v + 1] = fmaf(w, o4.y, acc[4 * v + 1]);
+              acc[4 * v + 2] = fmaf(w, o4.z, acc[4 * v + 2]);
+              acc[4 * v + 3] = fmaf(w, o4.w, acc[4 * v + 3]);
             }
-            w[e / 2] = pack_bf16x2(x0, x1);
           }
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+          store_row(c, acc, inv_l);
         }
       }
     }
@@ -488,18 +574,59 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 inline bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
 
+// Workspace of the tail split: counters, then (max, sum) rows, then O rows,
+// sized for one part per SM.
+constexpr int64_t kCounterBytes = 1024;
+inline int64_t split_bytes(int sms) {
+  return kCounterBytes + static_cast<int64_t>(sms) * 256 * (2 + kD) * sizeof(float);
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
 template <bool kSage>
-int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
-           int64_t bh, cudaStream_t st) {
+int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, Params p,
+           int64_t bh, void* ws, int64_t ws_bytes, cudaStream_t st) {
   using C = Cfg<kSage>;
   auto kernel = attention_kernel<kSage>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
       cudaSuccess)
     return XGB_ERR_LAUNCH;
-
-  dim3 grid(static_cast<unsigned>((p.seq_q + kQT * kBM - 1) / (kQT * kBM)),
-            static_cast<unsigned>(bh));
-  kernel<<<grid, kThreads, C::kSmem, st>>>(qm, km, vm, p);
+  // Work items: (batch*head, pair of 128-row Q tiles), one CTA each, one CTA
+  // per SM. The last, partial wave leaves SMs idle; its items are split
+  // along the KV range so that wave fills the SMs with shorter CTAs.
+  const int64_t n_qt = (p.seq_q + kQT * kBM - 1) / (kQT * kBM);
+  const int64_t items = n_qt * bh;
+  if (items > INT32_MAX / 2) return XGB_ERR_SHAPE;
+  const int sms = sm_count();
+  const int n_all = (p.seq_kv + kBN - 1) / kBN;
+  const int tail = static_cast<int>(items % sms);
+  int splits = 1;
+  if (ws && tail > 0 && ws_bytes >= split_bytes(sms) && tail * (int64_t)sizeof(int) <= kCounterBytes) {
+    splits = std::min(sms / tail, n_all);
+    if (splits > 1) {
+      const int per = (n_all + splits - 1) / splits;
+      splits = (n_all + per - 1) / per;  // no empty part
+    }
+  }
+  p.n_qt = static_cast<int>(n_qt);
+  p.splits = 1;
+  p.n_full = static_cast<int>(items);
+  if (splits > 1) {
+    char* w = static_cast<char*>(ws);
+    p.counters = reinterpret_cast<int*>(w);
+    p.part_ml = reinterpret_cast<float*>(w + kCounterBytes);
+    p.part_o = p.part_ml + static_cast<int64_t>(sms) * 256 * 2;
+    p.splits = splits;
+    p.n_full = static_cast<int>(items - tail);
+    if (cudaMemsetAsync(p.counters, 0, tail * sizeof(int), st) != cudaSuccess) return XGB_ERR_LAUNCH;
+  }
+  const int64_t grid = p.n_full + static_cast<int64_t>(items - p.n_full) * p.splits;
+  kernel<<<static_cast<unsigned>(grid), kThreads, C::kSmem, st>>>(qm, km, vm, p);
   return launch_status();
 }
 
@@ -520,7 +647,8 @@ using namespace xgb::attn;
 XGB_API int xgb_attention_sage(const int8_t* q8, const float* q_scale, const int8_t* k8,
                                const float* k_scale, const uint8_t* v8, const float* v_scale,
                                int64_t batch, int64_t heads, int64_t seq, void* out,
-                               const int64_t* out_strides, int* error_flag, void* stream) {
+                               const int64_t* out_strides, void* split_workspace,
+                               int64_t split_workspace_bytes, int* error_flag, void* stream) {
   if (!q8 || !q_scale || !k8 || !k_scale || !v8 || !v_scale || !out || !out_strides)
     return XGB_ERR_ARG;
   if (batch <= 0 || heads <= 0 || seq <= 0 || seq > (1 << 30) || batch * heads > 65535)
@@ -557,13 +685,14 @@ XGB_API int xgb_attention_sage(const int8_t* q8, const float* q_scale, const int
   p.osh = out_strides[1];
   p.oss = out_strides[2];
   p.err = error_flag;
-  return launch<true>(qm, km, vm, p, bh, as_stream(stream));
+  return launch<true>(qm, km, vm, p, bh, split_workspace, split_workspace_bytes, as_stream(stream));
 }
 
 XGB_API int xgb_attention_bf16(const void* q, const int64_t* q_strides, const void* k,
                                const int64_t* k_strides, const void* v, const int64_t* v_strides,
                                int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_kv,
                                float sm_scale, void* out, const int64_t* out_strides,
+                               void* split_workspace, int64_t split_workspace_bytes,
                                int* error_flag, void* stream) {
   if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || !out_strides)
     return XGB_ERR_ARG;
@@ -603,5 +732,8 @@ XGB_API int xgb_attention_bf16(const void* q, const int64_t* q_strides, const vo
   p.osh = out_strides[1];
   p.oss = out_strides[2];
   p.err = error_flag;
-  return launch<false>(qm, km, vm, p, batch * heads, as_stream(stream));
+  return launch<false>(qm, km, vm, p, batch * heads, split_workspace, split_workspace_bytes,
+                       as_stream(stream));
 }
+
+XGB_API int64_t xgb_attention_split_workspace_bytes(void) { return split_bytes(sm_count()); }
