@@ -56,6 +56,8 @@ def parse():
     # one-CTA-per-SM attention kernel slow it more than they hide, and
     # chunks of 3 heads quantize to 10.05 waves of 148 SMs.
     ap.add_argument("--phaa-num", type=int, default=1)
+    ap.add_argument("--wire", choices=("fp8", "int8"), default="fp8",
+                    help="SP gather transport (Sage): the FP8 wire, or Sage-quantised INT8")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-block", action="store_true", help="skip the full DiT block timing")
@@ -260,11 +262,14 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(world, precision):
-    return {"workload": "h3-sp-self-attention-768p5s", "seq_real": SEQ, "grid": list(GRID),
-            "text_tokens": TEXT, "audio_tokens": AUDIO, "heads": HEADS, "head_dim": HEAD_DIM,
-            "sp": world, "precision": precision, "parallelism": f"sp{world}",
-            "l2": "inputs larger than L2 (3 x S_loc x 3072 bf16 per rank)"}
+def workload_config(world, precision, wire="fp8"):
+    cfg = {"workload": "h3-sp-self-attention-768p5s", "seq_real": SEQ, "grid": list(GRID),
+           "text_tokens": TEXT, "audio_tokens": AUDIO, "heads": HEADS, "head_dim": HEAD_DIM,
+           "sp": world, "precision": precision, "parallelism": f"sp{world}",
+           "l2": "inputs larger than L2 (3 x S_loc x 3072 bf16 per rank)"}
+    if world > 1 and precision == "sage":
+        cfg["wire"] = wire
+    return cfg
 
 
 # ------------------------------------------------------------------ B200 arm
@@ -325,7 +330,8 @@ def main():
         return sp_self_attention(qq, kk, vv, (cos, sin), backend=backend, heads=HEADS,
                                  head_dim=HEAD_DIM, sp_group=group, sp_size=world,
                                  phaa_num=min(args.phaa_num, HEADS // world),
-                                 fp8_transport=fp8_wire, comm_stream=comm_stream)
+                                 fp8_transport=fp8_wire, comm_stream=comm_stream,
+                                 int8_transport=fp8_wire and args.wire == "int8")
 
     def barrier():
         if world > 1:
@@ -377,13 +383,14 @@ def main():
         block = block_timing(args, world, rank, dev, group, s_loc, cos, sin, comm_stream, barrier,
                              max_over_ranks)
 
-    kernels_per_layer = kernels_per_step(args.precision, world, min(args.phaa_num, HEADS // world))
+    kernels_per_layer = kernels_per_step(args.precision, world, min(args.phaa_num, HEADS // world),
+                                         args.wire)
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8/e4m3 (fp32 accumulate)" if args.precision == "sage" else "bf16",
-        "data": "synthetic", "config": workload_config(world, args.precision),
+        "data": "synthetic", "config": workload_config(world, args.precision, args.wire),
         "per_gpu_tflops": value / world, "attention_calls_per_step": attn_calls,
         "gpu_launches": kernels_per_layer * args.steps,
         "clocks": clocks.summary(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
@@ -446,13 +453,16 @@ def block_timing(args, world, rank, dev, group, s_loc, cos, sin, comm_stream, ba
             "config": "hidden 3072, 24x128 heads, FFN 12288 GELU, AdaLN LayerNorm, FP8 per-token linears"}
 
 
-def kernels_per_step(precision, world, phaa):
+def kernels_per_step(precision, world, phaa, wire="fp8"):
     """Our kernel launches per layer: SP=1: RoPE + (Sage: 3 prepare + 1 attention).
     SP>1 per PHAA chunk: QKV encode, decode, (Sage: 3 prepare) + attention,
-    return encode, decode."""
+    return encode, decode. INT8 wire (one chunk): stats, stats finalize,
+    encode, attention, return encode, decode."""
     attn = 4 if precision == "sage" else 1
     if world == 1:
         return 1 + attn
+    if precision == "sage" and wire == "int8":
+        return 6
     per_chunk = attn + (4 if precision == "sage" else 0)
     return phaa * per_chunk + (1 if precision != "sage" else 0)
 

@@ -282,6 +282,55 @@ int xgb_attention_sage(const int8_t* q8, const float* q_scale, const int8_t* k8,
  * workspace is used stream-ordered: launches that share it must not overlap. */
 int64_t xgb_attention_split_workspace_bytes(void);
 
+/* ---- Sage quantisation before the SP exchange ("INT8 on the wire") ---- */
+
+/* Per (peer, batch, head) of the rank's local rows, viewed like the FP8 wire
+ * sources as [peers, seq, batch, heads] rows of 128 bf16 channels (element
+ * strides *_strides[0..3], channel stride 1): channel sums of K after the
+ * partial RoPE (rotary channels, cos/sin [seq, rotary] fp32, rotary a
+ * multiple of 16 or 0) into ksum, and channel abs-maxima of V into vmax,
+ * both [peers*batch*heads][128] fp32, in a fixed order. The caller
+ * all-reduces them over the SP group (SUM, MAX) for sequence-wide values.
+ * Part of the B200 "INT8 on the wire" exchange that replaces the FP8 wire
+ * (x_base/x_base/phaa/fp8_transport.py:85-144) plus the attention-side
+ * Sage quantisation. */
+int64_t xgb_sage_wire_stats_workspace(int64_t peers, int64_t seq, int64_t batch, int64_t heads);
+int xgb_sage_wire_stats(const void* k, const int64_t* k_strides, const void* v,
+                        const int64_t* v_strides, int64_t peers, int64_t seq, int64_t batch,
+                        int64_t heads, const float* cos, const float* sin, int64_t rotary,
+                        float* ksum, float* vmax, void* workspace, int64_t workspace_bytes,
+                        void* stream);
+
+/* Quantise the rank's rows for the exchange (seq a multiple of 16): Q after
+ * RoPE times sm_scale*log2(e) and K after RoPE minus ksum/seq_real, int8
+ * per (head, group of 16 rows) with scale amax/127; V e4m3 per channel with
+ * scale max(vmax/448, FLT_MIN). Writes q8/k8/v8 [peers][seq][batch][heads]
+ * [128], qk_scale [peers][seq/16][batch][heads][2] (Q, K) and v_scale
+ * [peers*batch*heads][128]; after an A2A over the peer dimension the
+ * receiver passes them to xgb_attention_sage_strided unchanged. */
+int xgb_sage_wire_encode(const void* q, const int64_t* q_strides, const void* k,
+                         const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                         int64_t peers, int64_t seq, int64_t batch, int64_t heads,
+                         const float* cos, const float* sin, int64_t rotary, float sm_scale,
+                         const float* ksum, const float* vmax, int64_t seq_real, int8_t* q8,
+                         int8_t* k8, uint8_t* v8, float* qk_scale, float* v_scale, void* stream);
+
+/* xgb_attention_sage over quantised tensors in place: q8/k8/v8 rows of
+ * (b, h, s) at byte offsets b*st[0] + h*st[1] + s*st[2] (multiples of 16),
+ * Q/K scales per group of 16 rows at element offsets b*sst[0] + h*sst[1] +
+ * (s/16)*sst[2], V scale rows at b*vst[0] + h*vst[1]; scale_rows (>= seq, a
+ * multiple of 16) rows exist behind every (b, h); keys >= seq are masked.
+ * Output and split workspace as xgb_attention_sage. */
+int xgb_attention_sage_strided(const int8_t* q8, const int64_t* q_strides, const float* q_scale,
+                               const int64_t* q_scale_strides, const int8_t* k8,
+                               const int64_t* k_strides, const float* k_scale,
+                               const int64_t* k_scale_strides, const uint8_t* v8,
+                               const int64_t* v_strides, const float* v_scale,
+                               const int64_t* v_scale_strides, int64_t batch, int64_t heads,
+                               int64_t seq, int64_t scale_rows, void* out,
+                               const int64_t* out_strides, void* split_workspace,
+                               int64_t split_workspace_bytes, int* error_flag, void* stream);
+
 /* Non-causal BF16 attention (tcgen05 kind::f16, fp32 accumulation) reading
  * q [b, h, seq_q, 128] and k/v [b, h, seq_kv, 128] views in place through
  * TMA (strides in elements, multiples of 8, d stride 1), scale sm_scale.

@@ -64,6 +64,15 @@ SIGNATURES = {
                                  c_i64, c_i64, c_float, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                  c_i64, c_vp]),
     "xgb_attention_split_workspace_bytes": (c_i64, []),
+    "xgb_sage_wire_stats_workspace": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
+    "xgb_sage_wire_stats": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
+                                    c_i64, c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "xgb_sage_wire_encode": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_i64, c_i64, c_i64,
+                                     c_i64, c_vp, c_vp, c_i64, c_float, c_vp, c_vp, c_i64, c_vp,
+                                     c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "xgb_attention_sage_strided": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p,
+                                           c_vp, c_i64p, c_vp, c_i64p, c_i64, c_i64, c_i64, c_i64,
+                                           c_vp, c_i64p, c_vp, c_i64, c_vp, c_vp]),
     "xgb_attention_sage": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp,
                                    c_i64p, c_vp, c_i64, c_vp, c_vp]),
     "xgb_attention_bf16": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_i64, c_i64, c_i64,

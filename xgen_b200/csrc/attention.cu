@@ -121,6 +121,11 @@ struct Params {
   float* part_o;   // [tail CTAs][256][128]
   float* part_ml;  // [tail CTAs][256][2]
   int* counters;   // [tail items], zero at launch
+  // Sage wire layout (kWire): Q/K scales per group of 16 tokens, strided:
+  // the scale of (b, h, group g) sits at b*_b + h*_h + g*_g; the V scale row
+  // of (b, h) at b*vs_b + h*vs_h; scale_rows = token rows the scales cover.
+  int64_t qs_b, qs_h, qs_g, ks_b, ks_h, ks_g, vs_b, vs_h;
+  int scale_rows;
 };
 
 struct Barriers {
@@ -141,10 +146,12 @@ struct Barriers {
 __device__ __forceinline__ uint32_t s_col(int i, int b) { return static_cast<uint32_t>(i * 128 + b * 64); }
 __device__ __forceinline__ uint32_t o_col(int i) { return static_cast<uint32_t>(256 + i * 128); }
 
-template <bool kSage>
+template <bool kSage, bool kWire>
 __device__ __forceinline__ void load_rows(const CUtensorMap* map, uint8_t* dst, uint64_t* bar,
                                           int row, int bh, int heads, int sub_bytes) {
-  if constexpr (kSage) {
+  if constexpr (kSage && kWire) {
+    tma_load_4d(dst, map, bar, 0, row, bh % heads, bh / heads);
+  } else if constexpr (kSage) {
     tma_load_3d(dst, map, bar, 0, row, bh);
   } else {
     const int b = bh / heads, h = bh % heads;
@@ -171,7 +178,7 @@ __device__ __forceinline__ uint64_t vdesc(uint32_t tile_saddr, int k) {
   return smem_desc_sw128(tile_saddr + off, Cfg<kSage>::kSub, 1024);
 }
 
-template <bool kSage>
+template <bool kSage, bool kWire = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap q_map,
                      const __grid_constant__ CUtensorMap k_map,
@@ -230,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       mbar_arrive_expect_tx(&bars->q_full, kQT * C::kQBytes);
       for (int i = 0; i < kQT; ++i)
-        load_rows<kSage>(&q_map, smem + C::kQOff + i * C::kQBytes, &bars->q_full, m0 + i * kBM,
+        load_rows<kSage, kWire>(&q_map, smem + C::kQOff + i * C::kQBytes, &bars->q_full, m0 + i * kBM,
                          bh, p.heads, kBM * 128);
       int issued = 0;
       for (int t = 0; t < n_kv && ok; ++t) {
@@ -238,10 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t >= C::kStages) ok = mbar_wait(&bars->kv_empty[s], ((t / C::kStages) - 1) & 1, p.err);
         if (!ok) break;
         mbar_arrive_expect_tx(&bars->k_full[s], C::kKVBytes);
-        load_rows<kSage>(&k_map, smem + C::kKOff + s * C::kKVBytes, &bars->k_full[s], (kv0 + t) * kBN,
+        load_rows<kSage, kWire>(&k_map, smem + C::kKOff + s * C::kKVBytes, &bars->k_full[s], (kv0 + t) * kBN,
                          bh, p.heads, C::kSub);
         mbar_arrive_expect_tx(&bars->v_full[s], C::kKVBytes);
-        load_rows<kSage>(&v_map, smem + C::kVOff + s * C::kKVBytes, &bars->v_full[s], (kv0 + t) * kBN,
+        load_rows<kSage, kWire>(&v_map, smem + C::kVOff + s * C::kKVBytes, &bars->v_full[s], (kv0 + t) * kBN,
                          bh, p.heads, C::kSub);
         issued = t + 1;
       }
@@ -311,14 +318,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = m0 + i * kBM + lane_base + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lane_base) << 16);
     const uint32_t o_addr = lane_addr + o_col(i);
+    const int hb = bh / p.heads, hh = bh % p.heads;
     float qs = 0.f;
-    if constexpr (kSage) {
+    if constexpr (kSage && kWire) {
+      if (row < p.scale_rows) qs = p.q_scale[hb * p.qs_b + hh * p.qs_h + (row / 16) * p.qs_g];
+    } else if constexpr (kSage) {
       if (row < p.scale_stride * 64) qs = p.q_scale[static_cast<int64_t>(bh) * p.scale_stride + row / 64];
     }
     float m_used = kNegInf;
     float l = 0.f;
     float ks = 0.f;  // K-block scale of the current tile (Sage)
-    if constexpr (kSage) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0];
+    if constexpr (kSage && !kWire) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0];
+    // Wire layout: the four 16-key group scales of the current and next tile
+    // (groups past the last one read the last one; those keys are masked).
+    float ks4[4] = {0.f, 0.f, 0.f, 0.f}, ks4n[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* ksp = kWire ? p.k_scale + hb * p.ks_b + hh * p.ks_h : nullptr;
+    const int last_group = p.scale_rows / 16 - 1;
+    const int ks_g = static_cast<int>(p.ks_g);
+    auto load_ks4 = [&](int tile, float (&k)[4]) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) k[j] = __ldg(ksp + min(tile * 4 + j, last_group) * ks_g);
+    };
+    if constexpr (kSage && kWire) {
+      if (n_kv > 0) load_ks4(kv0, ks4n);
+    }
     bool ok = true;
     // The two warpgroups take turns in the MUFU-bound exp section so one's
     // exp overlaps the other's load/max/rescale work. The turn passes through
@@ -348,8 +371,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // sentinel far below any real score.
       const int valid = p.seq_kv - (kv0 + t) * kBN;
       const float comb = kSage ? qs * ks : p.scale_log2;
+      float comb4[4];
+      if constexpr (kSage && kWire) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          ks4[j] = ks4n[j];
+          comb4[j] = qs * ks4[j];
+        }
+        if (t + 1 < n_kv) load_ks4(kv0 + t + 1, ks4n);
+      }
       if constexpr (kSage) {
-        if (t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0 + t + 1];
+        if (!kWire && t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0 + t + 1];
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -363,8 +395,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; ++e)
             if (c * 32 + e >= valid) r[c][e] = sentinel;
       }
-      // Four independent 3-input max chains, then combined.
+      // Four independent 3-input max chains, then combined (wire layout: one
+      // chain per 16-key scale group, scaled by its own group scale).
       float m4[4];
+      float mt;
+      if constexpr (kSage && kWire) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = j >> 1, e0 = (j & 1) * 16;
+          float m = fmax3(__uint_as_float(r[c][e0]), __uint_as_float(r[c][e0 + 1]), __uint_as_float(r[c][e0 + 2]));
+#pragma unroll
+          for (int e = e0 + 3; e < e0 + 15; e += 2)
+            m = fmax3(m, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]));
+          m4[j] = comb4[j] * (fmaxf(m, __uint_as_float(r[c][e0 + 15])) - 12582912.0f);
+        }
+        mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      } else {
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         m4[2 * c] = fmax3(__uint_as_float(r[c][0]), __uint_as_float(r[c][1]), __uint_as_float(r[c][2]));
@@ -377,7 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         m4[2 * c] = fmax3(m4[2 * c], __uint_as_float(r[c][30]), __uint_as_float(r[c][31]));
       }
       const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      const float mt = kSage ? comb * (mx - 12582912.0f) : mx * comb;
+      mt = kSage ? comb * (mx - 12582912.0f) : mx * comb;
+      }
       // Lazy rescale (warp-uniform TMEM traffic); O must hold PV(t-1).
       const float m_new = fmaxf(m_used, mt);
       const bool need = m_new > m_used + C::kTau;
@@ -408,14 +455,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       float rsa[4] = {0.f, 0.f, 0.f, 0.f}, rsb[4] = {0.f, 0.f, 0.f, 0.f};
       if constexpr (kSage) {
         const float off = (kLog2PScale - m_used) - 12582912.0f * comb;
+        float offs[4];
+        if constexpr (kWire) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) offs[j] = (kLog2PScale - m_used) - 12582912.0f * comb4[j];
+        }
         uint32_t packed[16];  // 64 keys of e4m3 P = 16 TMEM columns
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
             float x[4], pv[4];
-            ffma2(x[0], x[1], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb, off, off);
-            ffma2(x[2], x[3], __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]), comb, comb, off, off);
+            const float cb = kWire ? comb4[c * 2 + e / 16] : comb;
+            const float of = kWire ? offs[c * 2 + e / 16] : off;
+            ffma2(x[0], x[1], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), cb, cb, of, of);
+            ffma2(x[2], x[3], __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]), cb, cb, of, of);
 #pragma unroll
             for (int u = 0; u < 4; u += 2) {
               if (poly_pair((c * 32 + e + u) / 2)) {
@@ -469,9 +523,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // pv_done may trail the last tile by two phases here, so a parity wait
     // on it would be ambiguous; o_done completes exactly once.
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[i], 0, p.err));
-    const int b = bh / p.heads, h = bh % p.heads;
-    __nv_bfloat16* dst = p.out + b * p.osb + h * p.osh + static_cast<int64_t>(row) * p.oss;
-    const float* vsc = kSage ? p.v_scale + static_cast<int64_t>(bh) * kD : nullptr;
+    __nv_bfloat16* dst = p.out + hb * p.osb + hh * p.osh + static_cast<int64_t>(row) * p.oss;
+    const float* vsc = !kSage ? nullptr
+                       : kWire ? p.v_scale + hb * p.vs_b + hh * p.vs_h
+                               : p.v_scale + static_cast<int64_t>(bh) * kD;
     // out row = o / l (times the per-channel V scale for Sage), as bf16.
     auto store_row = [&](int c, const float* o, float inv_l) {
       uint32_t w[16];
@@ -588,11 +643,11 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <bool kSage>
+template <bool kSage, bool kWire = false>
 int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, Params p,
            int64_t bh, void* ws, int64_t ws_bytes, cudaStream_t st) {
   using C = Cfg<kSage>;
-  auto kernel = attention_kernel<kSage>;
+  auto kernel = attention_kernel<kSage, kWire>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
       cudaSuccess)
     return XGB_ERR_LAUNCH;
@@ -737,3 +792,64 @@ XGB_API int xgb_attention_bf16(const void* q, const int64_t* q_strides, const vo
 }
 
 XGB_API int64_t xgb_attention_split_workspace_bytes(void) { return split_bytes(sm_count()); }
+
+XGB_API int xgb_attention_sage_strided(
+    const int8_t* q8, const int64_t* q_strides, const float* q_scale, const int64_t* q_scale_strides,
+    const int8_t* k8, const int64_t* k_strides, const float* k_scale, const int64_t* k_scale_strides,
+    const uint8_t* v8, const int64_t* v_strides, const float* v_scale,
+    const int64_t* v_scale_strides, int64_t batch, int64_t heads, int64_t seq, int64_t scale_rows,
+    void* out, const int64_t* out_strides, void* split_workspace, int64_t split_workspace_bytes,
+    int* error_flag, void* stream) {
+  if (!q8 || !k8 || !v8 || !q_scale || !k_scale || !v_scale || !out) return XGB_ERR_ARG;
+  if (!q_strides || !k_strides || !v_strides || !q_scale_strides || !k_scale_strides ||
+      !v_scale_strides || !out_strides)
+    return XGB_ERR_ARG;
+  if (batch <= 0 || heads <= 0 || seq <= 0 || seq > (1 << 30) || scale_rows < seq ||
+      scale_rows % 16 || scale_rows > (1 << 30))
+    return XGB_ERR_SHAPE;
+  if (out_strides[3] != 1 || out_strides[2] % 8 || out_strides[1] % 8 || out_strides[0] % 8)
+    return XGB_ERR_STRIDE;
+  const int64_t* in[3] = {q_strides, k_strides, v_strides};
+  for (auto st : in)
+    for (int d = 0; d < 3; ++d)
+      if (st[d] % 16 || st[d] <= 0) return XGB_ERR_STRIDE;  // 16-byte TMA strides (1-byte elements)
+  if (!aligned(q8, 16) || !aligned(k8, 16) || !aligned(v8, 16) || !aligned(out, 16))
+    return XGB_ERR_ALIGN;
+  int rc = check_device();
+  if (rc) return rc;
+  CUtensorMap qm, km, vm;
+  auto make = [&](CUtensorMap* m, const void* base, const int64_t* s, uint32_t rows) {
+    const uint32_t box[4] = {128, rows, 1, 1};
+    const uint64_t dims[4] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(scale_rows),
+                              static_cast<uint64_t>(heads), static_cast<uint64_t>(batch)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(s[2]), static_cast<uint64_t>(s[1]),
+                                 static_cast<uint64_t>(s[0])};
+    return make_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, box);
+  };
+  if (!make(&qm, q8, q_strides, kBM) || !make(&km, k8, k_strides, kBN) || !make(&vm, v8, v_strides, kBN))
+    return XGB_ERR_ALIGN;
+  Params p{};
+  p.q_scale = q_scale;
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  p.heads = static_cast<int>(heads);
+  p.seq_q = static_cast<int>(seq);
+  p.seq_kv = static_cast<int>(seq);
+  p.scale_log2 = 1.0f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.osb = out_strides[0];
+  p.osh = out_strides[1];
+  p.oss = out_strides[2];
+  p.err = error_flag;
+  p.qs_b = q_scale_strides[0];
+  p.qs_h = q_scale_strides[1];
+  p.qs_g = q_scale_strides[2];
+  p.ks_b = k_scale_strides[0];
+  p.ks_h = k_scale_strides[1];
+  p.ks_g = k_scale_strides[2];
+  p.vs_b = v_scale_strides[0];
+  p.vs_h = v_scale_strides[1];
+  p.scale_rows = static_cast<int>(scale_rows);
+  return launch<true, true>(qm, km, vm, p, batch * heads, split_workspace, split_workspace_bytes,
+                            as_stream(stream));
+}

@@ -20,10 +20,18 @@ from ..sp.comm import all_to_all_after_attn, all_to_all_before_attn
 def sp_self_attention(query, key, value, rotary_emb, *, backend, heads: int, head_dim: int = 128,
                       sp_group=None, sp_size: int = 1, phaa_num: int = 2,
                       fp8_transport: bool = True, comm_stream=None, pad_key: str = "mmh3_seq",
-                      device_join: bool = True, use_phaa: bool = True):
-    """query/key/value (B, S_loc, heads*head_dim) bf16 -> (B, S_loc, heads*head_dim)."""
+                      device_join: bool = True, use_phaa: bool = True, int8_transport: bool = False):
+    """query/key/value (B, S_loc, heads*head_dim) bf16 -> (B, S_loc, heads*head_dim).
+    int8_transport: Sage-quantise before the exchange (xgen_b200.phaa.sage_wire)
+    and return the output over the FP8 wire."""
     b, s, _ = query.shape
     with torch.no_grad():
+        if sp_size > 1 and int8_transport:
+            return run_phaa_attention(
+                query, key, value, comm_stream=comm_stream, sp_group=sp_group, sp_size=sp_size,
+                heads=heads, phaa_split_num=1, head_dim=head_dim, rotary_emb=rotary_emb,
+                pad_key=pad_key, attention_fn=backend, fp8_transport=True,
+                device_join=device_join, int8_transport=True)
         if sp_size > 1 and use_phaa:
             if not fp8_transport and rotary_emb is not None:
                 query, key = _rope(query, key, rotary_emb, heads, head_dim)

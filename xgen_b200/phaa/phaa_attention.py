@@ -14,9 +14,15 @@ device join) every exchange is an async NCCL collective submitted on
 `finish_fp8_exchange`), optionally with the direct gather, fused return pack
 and direct return layouts (phaa_attention.py:84-107, :150-327).
 
-B200 extension: `fuse_rope=True` with `rotary_emb=(cos, sin)` applies the
-partial RoPE to Q and K inside the FP8 wire encode (the reference applies it
-in a separate pass before PHAA; the bytes on the wire are identical).
+B200 extensions:
+- `fuse_rope=True` with `rotary_emb=(cos, sin)` applies the partial RoPE to Q
+  and K inside the FP8 wire encode (the reference applies it in a separate
+  pass before PHAA; the bytes on the wire are identical).
+- `int8_transport=True` (one head chunk, the B200 Sage backend) sends Q/K/V
+  already Sage-quantised (`sage_wire`: RoPE, int8 Q/K per 16 tokens, e4m3 V
+  per channel, sequence-wide K mean and V scale from an all-reduce) and runs
+  the attention on the received bytes in place; the output returns over the
+  FP8 wire (`fp8_transport=True`) or bf16.
 """
 from __future__ import annotations
 
@@ -68,7 +74,7 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
                        attention_mask=None, pad_key="pad", attention_fn=None,
                        fp8_transport=False, gather_priority=False, scatter_stream=None,
                        scatter_group=None, tail_first=False, device_join=False,
-                       async_options=None, fuse_rope=False):
+                       async_options=None, fuse_rope=False, int8_transport=False):
     """query/key/value (B, S_loc, heads*head_dim) -> (B, S_loc, heads*head_dim)."""
     W_S = sp_size
     B, Sq, H = query.shape
@@ -92,6 +98,12 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
         raise ValueError("Separate PHAA scatter requires FP8, a stream and a process group")
     if fp8_transport and query.device.type != "cuda":
         raise ValueError("PHAA FP8 transport requires CUDA")
+    if int8_transport:
+        return _int8_wire(query, key, value, comm_stream=comm_stream, sp_group=sp_group,
+                          sp_size=sp_size, heads=heads, phaa_split_num=phaa_split_num,
+                          head_dim=head_dim, rotary_emb=rotary_emb, attention_mask=attention_mask,
+                          pad_key=pad_key, attention_fn=attention_fn, fp8_transport=fp8_transport,
+                          device_join=device_join)
 
     hpd = heads // W_S
     sizes = chunk_sizes(hpd, phaa_split_num)
@@ -233,3 +245,53 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
     if direct_return:
         return final
     return torch.cat([b.permute(2, 1, 0, 3) for b in returned], dim=3).flatten(-2, -1)
+
+
+def _int8_wire(query, key, value, *, comm_stream, sp_group, sp_size, heads, phaa_split_num,
+               head_dim, rotary_emb, attention_mask, pad_key, attention_fn, fp8_transport,
+               device_join):
+    """PHAA with the INT8 wire: one chunk of all local heads (see module doc)."""
+    from .sage_wire import SageWire, sage_wire_attention, sage_wire_exchange
+
+    if phaa_split_num != 1:
+        raise ValueError("INT8 wire transport exchanges all local heads at once (phaa_split_num=1)")
+    if getattr(attention_fn, "precision", None) != "sage" or attention_mask is not None:
+        raise ValueError("INT8 wire transport needs the B200 Sage backend and no attention mask")
+    if query.device.type != "cuda" or head_dim != 128:
+        raise ValueError("INT8 wire transport needs CUDA and head_dim 128")
+    W = sp_size
+    B, Sq, H = query.shape
+    hpd = heads // W
+    pad = get_pad_manager().get_or_default(pad_key, 0)
+    seq_real = W * Sq - pad
+    rank = dist.get_rank(sp_group) if W > 1 else 0
+    cur = torch.cuda.current_stream(query.device)
+    # Buffers belong to the compute stream, which waits for the exchange
+    # before reading them, so their reuse stays ordered after it.
+    bufs = SageWire(W, Sq, B, hpd, query.device)
+    comm_stream.wait_stream(cur)
+    with torch.cuda.stream(comm_stream):
+        sage_wire_exchange(query, key, value, heads=heads, group=sp_group, peers=W,
+                           rotary_emb=rotary_emb, seq_real=seq_real, bufs=bufs)
+    cur.wait_stream(comm_stream)
+    send = torch.empty((W, Sq, B, hpd, head_dim), device=query.device, dtype=query.dtype)
+    if pad > 0:
+        send[-1, Sq - pad:].zero_()
+    view = send.flatten(0, 1).permute(1, 2, 0, 3).narrow(2, 0, W * Sq - pad)
+    sage_wire_attention(bufs, view, seq_real, rank)
+    attention_fn.calls += 1
+    attention_fn.kernel_calls += 1
+    returned = torch.empty((W, Sq, B, hpd * head_dim), device=query.device, dtype=query.dtype)
+    comm_stream.wait_stream(cur)
+    with torch.cuda.stream(comm_stream):
+        if fp8_transport:
+            fp8.fp8_all_to_all(returned, send.flatten(-2, -1), head_dim, sp_group)
+        else:
+            dist.all_to_all_single(returned, send.flatten(-2, -1), group=sp_group)
+        for t in (query, key, value, send):
+            t.record_stream(comm_stream)
+    if device_join:
+        cur.wait_stream(comm_stream)
+    else:
+        comm_stream.synchronize()
+    return returned.permute(2, 1, 0, 3).flatten(-2, -1)
