@@ -28,7 +28,7 @@ import sys
 import tempfile
 import threading
 import time
-from datetime import timedelta
+from datetime import datetime, timedelta
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -155,9 +155,14 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled during the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    The sampler starts (and is waited for until its first sample) before the
+    region; `mark_start()` / `mark_end()` bracket the region and only samples
+    time-stamped inside it count. The interval is 20 ms, so even the ~90 ms
+    regions of an 8-GPU run get several samples."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -165,6 +170,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -172,19 +178,36 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            deadline = time.time() + 5.0
+            while time.time() < deadline and not Path(self.path).read_text().strip():
+                time.sleep(0.02)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.05)  # let the sample covering the region's end land
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+
+    @staticmethod
+    def _when(stamp: str) -> float | None:
+        try:
+            return datetime.strptime(stamp.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def summary(self):
         if self.proc is None or not self.path:
@@ -192,16 +215,20 @@ class ClockSampler:
         rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and parts[1].isdigit():
+            if len(parts) >= 10 and parts[2].isdigit():
                 rows.append(parts)
         os.unlink(self.path)
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if (w := self._when(r[0])) is not None
+                      and self.t0 - 0.02 <= w <= self.t1 + 0.02]
+            rows = inside or rows
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [int(r[1]) for r in rows]
+        sm = [int(r[2]) for r in rows]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]),
-                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][3]),
+                "power_w_max": max(float(r[4]) for r in rows if r[4].replace(".", "").isdigit()),
                 "samples": len(rows), "reasons": reasons}
 
 
@@ -353,11 +380,13 @@ def main():
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         barrier()
+        clocks.mark_start()
         start.record()
         for _ in range(args.steps):
             out = step(q, k, v)
         end.record()
         barrier()
+        clocks.mark_end()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     attn_calls = (backend.kernel_calls - launches_before) // args.steps
     assert kernel_errors(dev) == 0, "a tcgen05 kernel reported a timed-out wait"
