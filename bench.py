@@ -316,6 +316,7 @@ def main():
     from xgen_b200.attention import H3AttentionBackendB200, kernel_errors
     from xgen_b200.h3.rope import rope_3d
     from xgen_b200.h3.sp_attention import sp_self_attention
+    from xgen_b200.sp.mesh import ParallelManager
     from xgen_b200.sp.padding import get_pad_manager
 
     rank, world, local = dist_env()
@@ -326,7 +327,8 @@ def main():
     group = None
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-        group = dist.group.WORLD
+        # the H3 enable_parallel mesh: every GPU of the job in one SP group
+        group = ParallelManager(1, 1, world, 1).sp_group
     _lib.lib()
 
     # Workload: pad the packed sequence to a multiple of 16*SP.

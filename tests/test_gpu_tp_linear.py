@@ -11,6 +11,8 @@ import torch.distributed as dist
 
 pytestmark = pytest.mark.gpu
 
+_GROUP = object()  # an explicit TP group; every collective on it is patched below
+
 
 def test_group_scale_quantisation(cuda_device):
     from xgen_b200.ops import quantize_activation
@@ -51,7 +53,7 @@ def test_column_parallel_gather(cuda_device):
     b0, b1 = b.chunk(2)
     ref1 = H3FP8Linear(w1, b1).to(cuda_device)(x)  # rank 1's local output
     layer = H3FP8TPLinear(SimpleNamespace(weight=w0, bias=b0, column_parallel=True,
-                                          gather_output=True, tp_group=None)).to(cuda_device)
+                                          gather_output=True, tp_group=_GROUP)).to(cuda_device)
 
     def gather(values, output, group=None):
         values[0].copy_(output)
@@ -84,7 +86,7 @@ def test_row_parallel_slices_reduces_and_adds_bias_after(cuda_device):
         part1 = other(x1)
 
     layer = H3FP8TPLinear(SimpleNamespace(weight=w0, bias=b, column_parallel=False,
-                                          input_is_parallel=False, tp_group=None)).to(cuda_device)
+                                          input_is_parallel=False, tp_group=_GROUP)).to(cuda_device)
     layer.activation_group = object()
     calls = []
 
@@ -106,3 +108,35 @@ def test_row_parallel_slices_reduces_and_adds_bias_after(cuda_device):
     with patch.object(dist, "all_reduce", side_effect=lambda t, op=None, group=None: t.copy_(shared)):
         part0 = own(x0)
     assert torch.equal(out, (part0 + part1) + b.to(cuda_device))
+
+
+def test_group_falls_back_to_registered_tp_state(cuda_device):
+    """tp_group None: the layer uses the group ParallelManager registered, and
+    with none registered it runs unsharded without a collective
+    (x_base/x_base/tensor_parallelism/layers.py:17-27)."""
+    from xgen_b200 import tp_state
+    from xgen_b200.fp8_linear import H3FP8Linear, H3FP8TPLinear
+
+    w, b, x = _shards(cuda_device, seed=5)
+    w0, w1 = w.chunk(2, dim=0)
+    b0, b1 = b.chunk(2)
+    ref0 = H3FP8Linear(w0, b0).to(cuda_device)(x)
+    ref1 = H3FP8Linear(w1, b1).to(cuda_device)(x)
+    layer = H3FP8TPLinear(SimpleNamespace(weight=w0, bias=b0, column_parallel=True,
+                                          gather_output=True, tp_group=None)).to(cuda_device)
+    seen = []
+
+    def gather(values, output, group=None):
+        seen.append(group)
+        values[0].copy_(output)
+        values[1].copy_(ref1)
+
+    with patch.object(dist, "all_gather", side_effect=gather):
+        assert torch.equal(layer(x), ref0) and not seen  # nothing registered
+        tp_state.set_tp_group(_GROUP, 2, 0)
+        try:
+            out = layer(x)
+        finally:
+            tp_state.clear_tp_group()
+    assert seen == [_GROUP]
+    assert torch.equal(out, torch.cat([ref0, ref1], dim=-1))

@@ -197,7 +197,10 @@ class H3FP8TPLinear(H3FP8Linear):
 
     `original` carries weight/bias and the TP attributes `column_parallel`
     (or is an instance named ColumnParallelLinear), `gather_output`,
-    `input_is_parallel`, `tp_group`, `reduce_fn`."""
+    `input_is_parallel`, `tp_group`, `reduce_fn`. With `tp_group` None the
+    layer uses the group `ParallelManager` registered (xgen_b200.tp_state),
+    and runs unsharded when none is registered, as the reference's TP layers
+    do."""
 
     def __init__(self, original, scaling: str = "per_tensor"):
         bias = getattr(original, "bias", None)
@@ -213,10 +216,11 @@ class H3FP8TPLinear(H3FP8Linear):
     def forward(self, x):
         import torch.distributed as dist
 
-        group = self.tp_group
-        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        from . import tp_state
+
+        group, world, rank = tp_state.resolve(self.tp_group)
         if not self.column_parallel and not self.input_is_parallel and world > 1:
-            x = x.chunk(world, dim=-1)[dist.get_rank(group)]
+            x = x.chunk(world, dim=-1)[rank]
         bias = self.bias
         if not self.column_parallel:
             self.bias = None  # row bias belongs after the reduction

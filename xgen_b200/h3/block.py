@@ -76,6 +76,12 @@ class H3DiTBlockB200:
             self.norm_q.weight.data.copy_(weights["norm_q.weight"])
             self.norm_k.weight.data.copy_(weights["norm_k.weight"])
         self.attention = H3AttentionBackendB200(c.precision)
+        self.parallel_manager = None
+
+    def set_parallel_manager(self, parallel_manager) -> None:
+        """Attach a ParallelManager whose SP group every forward uses
+        (x_comfyui/x_comfyui/framework/transformer/minimax_h3.py:222-227)."""
+        self.parallel_manager = parallel_manager
 
     @staticmethod
     def random_weights(config: H3BlockConfig, seed: int = 0, std: float = 0.02) -> dict:
@@ -99,8 +105,16 @@ class H3DiTBlockB200:
         return w
 
     def forward(self, x, adaln_table, adaln_indices, rotary_emb, *, sp_group=None, sp_size=1,
-                phaa_num=2, fp8_transport=True, comm_stream=None, pad_key="mmh3_seq"):
-        """x [B, S_loc, hidden] bf16 -> [B, S_loc, hidden] bf16."""
+                phaa_num=2, fp8_transport=True, comm_stream=None, pad_key="mmh3_seq",
+                parallel_manager=None):
+        """x [B, S_loc, hidden] bf16 -> [B, S_loc, hidden] bf16. A
+        `parallel_manager` (argument, else the `parallel_manager` attribute
+        set_parallel_manager attaches) supplies the SP group and size, as the
+        reference's H3 attention reads them (x_comfyui/x_comfyui/framework/
+        transformer/minimax_h3.py:143-147)."""
+        pm = parallel_manager if parallel_manager is not None else self.parallel_manager
+        if pm is not None:
+            sp_group, sp_size = pm.sp_group, pm.sp_size
         c = self.config
         b, s, h = x.shape
         t = adaln_table

@@ -10,8 +10,10 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 from typing import Dict, Optional
 
+from .errors import SequenceParallelError
 
-class PadNotSetError(KeyError):
+
+class PadNotSetError(SequenceParallelError, KeyError):
     """Raised when a padding key is read before it was set
     (x_base/x_base/sequence_parallelism/errors.py:17)."""
 
