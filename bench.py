@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--linear-only", action="store_true",
                     help="time the FP8 Linear stack of one block (BASELINE config 4)")
     ap.add_argument("--sp", type=int, default=8, help="SP degree that sets the linear-stack M")
+    ap.add_argument("--hbm-kernels", action="store_true",
+                    help="time the HBM-bound kernels at one SP rank's shapes (--sp) against the measured HBM copy bandwidth")
     return ap.parse_args()
 
 
@@ -144,6 +146,114 @@ def kernel_only(args):
     assert kernel_errors(dev) == 0
     print(json.dumps({"kernel": f"attention_{args.precision}", "seq": args.seq, "heads": args.heads,
                       "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
+
+
+def hbm_kernels(args):
+    """The HBM-bound kernels of one SP rank at 768P-5s (--sp, default 8),
+    each timed alone with CUDA events around every launch and a 512 MB
+    write between launches, so no input is still in L2. Algorithmic bytes
+    are each kernel's compulsory reads and writes (every input read once,
+    every output written once); GB/s is compared with MEASURED_PEAKS.json's
+    copy bandwidth. Prints one JSON line."""
+    import torch
+
+    from xgen_b200 import ops
+    from xgen_b200.attention import SageWorkspace, kernel_errors, sage_prepare
+    from xgen_b200.h3.rope import rope_3d
+    from xgen_b200.phaa import fp8_transport as wire
+
+    dev = torch.device("cuda", 0)
+    sp = max(1, args.sp)
+    s_pad = -(-SEQ // (16 * sp)) * (16 * sp)
+    s_loc, hl, width = s_pad // sp, HEADS // sp, HEADS * HEAD_DIM
+    m = -(-SEQ // sp)  # linear-stack rows (BASELINE config 4)
+    hid, ffn = 3072, 12288
+    g = torch.Generator(device=dev).manual_seed(11)
+    rnd = lambda *shape: torch.randn(*shape, device=dev, generator=g).bfloat16()  # noqa: E731
+    cos, sin = (t[:s_loc].contiguous().to(dev) for t in rope_3d(GRID, TEXT + AUDIO))
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(run):
+        for _ in range(max(3, args.warmup)):
+            run()
+        total = 0.0
+        for _ in range(max(1, args.steps)):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            run()
+            e.record()
+            torch.cuda.synchronize()
+            total += s.elapsed_time(e)
+        return total / max(1, args.steps)
+
+    rows = {}
+
+    def record(name, nbytes, ms, shape):
+        rows[name] = {"ms": ms, "bytes": int(nbytes), "gbs": nbytes / ms / 1e6, "shape": shape}
+
+    # PHAA FP8 wire: encode with fused RoPE (3 streams, 8 peers), decode
+    # the [peer, S_loc, B, H_loc, D] views PHAA hands the codec (one head chunk)
+    qkv = [rnd(1, s_loc, width).unflatten(-1, (HEADS, HEAD_DIM)).unflatten(2, (sp, hl)).permute(2, 1, 0, 3, 4)
+           for _ in range(3)]
+    payload = 3 * s_loc * HEADS * (HEAD_DIM + 4)
+    buf = wire.encode(qkv, HEAD_DIM, sp, rotary_emb=(cos, sin))
+    ms = timed(lambda: wire.encode(qkv, HEAD_DIM, sp, rotary_emb=(cos, sin), out=buf))
+    record("fp8_wire_encode_rope", 3 * s_loc * width * 2 + 2 * cos.numel() * 4 + payload, ms,
+           f"3 x [1, {s_loc}, {width}] bf16 -> {sp} peers")
+    gathered = [torch.empty(sp, s_loc, 1, hl, HEAD_DIM, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    ms = timed(lambda: wire.decode(buf, gathered, HEAD_DIM, sp))
+    record("fp8_wire_decode", payload + 3 * s_loc * width * 2, ms, f"-> 3 x [{sp}, {s_loc}, 1, {hl}, 128] bf16")
+    del qkv, buf
+
+    # Sage preparation on the gathered layout (strided [B, H, S_real, D] views)
+    views = [t.permute(2, 3, 0, 1, 4).flatten(2, 3)[:, :, :SEQ] for t in gathered]
+    ws = SageWorkspace(1, hl, SEQ, dev)
+    ms = timed(lambda: sage_prepare(*views, ws=ws))
+    n = hl * SEQ * HEAD_DIM
+    record("sage_prep", 3 * n * 2 + 3 * n + (2 * ws.q_scale.numel() + ws.v_scale.numel()) * 4, ms,
+           f"3 x [1, {hl}, {SEQ}, 128] bf16 (gathered views)")
+    del views, ws, gathered
+
+    # standalone partial RoPE and Q/K RMSNorm + RoPE on [1, S_loc, H, D]
+    q4, k4 = rnd(1, s_loc, HEADS, HEAD_DIM), rnd(1, s_loc, HEADS, HEAD_DIM)
+    with torch.no_grad():
+        ms = timed(lambda: ops.try_h3_partial_rope(q4, k4, cos, sin))
+        record("partial_rope", 4 * q4.numel() * 2 + 2 * cos.numel() * 4, ms, f"2 x [1, {s_loc}, 24, 128] bf16")
+        nq = torch.nn.RMSNorm(HEAD_DIM, eps=1e-6).to(dev, torch.bfloat16)
+        nk = torch.nn.RMSNorm(HEAD_DIM, eps=1e-6).to(dev, torch.bfloat16)
+        ms = timed(lambda: ops.try_h3_qk_rms(q4, k4, nq, nk, rotary_emb=(cos, sin)))
+        record("qk_rms_rope", 4 * q4.numel() * 2 + 2 * cos.numel() * 4, ms, f"2 x [1, {s_loc}, 24, 128] bf16")
+    del q4, k4
+
+    # block elementwise: fused norm/modulate/quant, gated residual, FFN quant, SwiGLU
+    x = rnd(1, m, hid)
+    table = rnd(3, 6 * hid)
+    idx = torch.randint(0, 3, (m,), device=dev, generator=g)
+    ms = timed(lambda: ops.norm_modulate_quant(x, "layernorm", None, 1e-6, table[:, hid:2 * hid],
+                                               table[:, :hid], idx))
+    record("norm_modulate_quant", x.numel() * 2 + x.numel() + m * 4 + m * 8, ms, f"[1, {m}, {hid}] bf16 -> e4m3")
+    res = rnd(1, m, hid)
+    ms = timed(lambda: ops.indexed_affine(x, table[:, 2 * hid:3 * hid], res, idx, modulation=False))
+    record("indexed_affine_gate", 3 * x.numel() * 2 + m * 8, ms, f"[1, {m}, {hid}] bf16")
+    del x, res
+    hmat = rnd(m, ffn)
+    ms = timed(lambda: ops.quantize_per_token(hmat))
+    record("fp8_quantize_per_token", hmat.numel() * 3 + m * 4, ms, f"[{m}, {ffn}] bf16 -> e4m3")
+    del hmat
+    up = rnd(m, 2 * ffn)
+    ms = timed(lambda: ops.gate_first_swiglu(up))
+    record("swiglu", up.numel() * 2 + up.numel(), ms, f"[{m}, {2 * ffn}] -> [{m}, {ffn}] bf16")
+    del up
+    torch.cuda.synchronize()
+    assert kernel_errors(dev) == 0
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    for r in rows.values():
+        r["frac"] = r["gbs"] / peak
+    print(json.dumps({"hbm_kernels": rows, "sp": sp, "peak_gbs": peak,
+                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6650 GB/s",
+                      "l2": "512 MB write between launches"}), flush=True)
 
 
 # ------------------------------------------------------------------ helpers
@@ -306,6 +416,8 @@ def main():
         return run_reference(args)
     if args.kernel_only:
         return kernel_only(args)
+    if args.hbm_kernels:
+        return hbm_kernels(args)
     if args.linear_only:
         return linear_stack(args)
 

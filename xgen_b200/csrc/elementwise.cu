@@ -42,36 +42,33 @@ __device__ __forceinline__ float rope_channel(float x, float partner, bool first
 // ---------------------------------------------------------------- RoPE
 // Vector path: 8 channels per thread; requires width % 8 == 0 and
 // (rotary / 2) % 8 == 0 so a vector never straddles the rotary boundary or
-// the half split, and its partner vector is 16-byte aligned.
+// the half split, and its partner vector is 16-byte aligned. Thread u owns
+// chunk u of 8 channels; its (row, channel, position) come from 32-bit
+// invariant divisions.
 __global__ void __launch_bounds__(kThreads) partial_rope_vec_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
     const float* __restrict__ cos, const float* __restrict__ sin, __nv_bfloat16* __restrict__ qo,
-    __nv_bfloat16* __restrict__ ko, int64_t n, int64_t seq, int64_t heads, int64_t width,
-    int64_t rotary) {
+    __nv_bfloat16* __restrict__ ko, uint32_t chunks, FastDiv div_cpr, FastDiv div_heads,
+    FastDiv div_seq, int rotary) {
   const bool is_key = blockIdx.y == 1;
   const __nv_bfloat16* src = is_key ? k : q;
   __nv_bfloat16* dst = is_key ? ko : qo;
-  const int64_t e = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 8;
-  if (e >= n) return;
-  const int64_t ch = e % width;
-  Bf16x8 x = load8(src + e);
+  const uint32_t u = blockIdx.x * kThreads + threadIdx.x;
+  if (u >= chunks) return;
+  const uint32_t row = fast_div(u, div_cpr);
+  const int ch = static_cast<int>(u - row * div_cpr.d) * 8;
+  const int64_t e = static_cast<int64_t>(u) * 8;
+  uint4 x = __ldg(reinterpret_cast<const uint4*>(src + e));
   if (ch < rotary) {
-    const int64_t half = rotary / 2;
+    const int half = rotary / 2;
     const bool first = ch < half;
-    const int64_t s = (e / (heads * width)) % seq;
-    const Bf16x8 p = load8(src + e + (first ? half : -half));
-    const float4* cp = reinterpret_cast<const float4*>(cos + s * rotary + ch);
-    const float4* sp = reinterpret_cast<const float4*>(sin + s * rotary + ch);
-    const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
-    const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float r = rope_channel(__bfloat162float(x.v[i]), __bfloat162float(p.v[i]), first, cv[i], sv[i]);
-      x.v[i] = __float2bfloat16_rn(r);
-    }
+    const uint32_t bs = fast_div(row, div_heads);  // batch * seq + s
+    const uint32_t s = bs - fast_div(bs, div_seq) * div_seq.d;
+    const uint4 p = __ldg(reinterpret_cast<const uint4*>(src + e + (first ? half : -half)));
+    x = rope8_bf16(x, p, first, cos + static_cast<int64_t>(s) * rotary + ch,
+                   sin + static_cast<int64_t>(s) * rotary + ch);
   }
-  store8(dst + e, x);
+  *reinterpret_cast<uint4*>(dst + e) = x;
 }
 
 // Scalar path for any even rotary <= width.
@@ -148,6 +145,68 @@ __global__ void __launch_bounds__(kThreads) qk_rms_kernel(
     }
     dst[c] = __float2bfloat16_rn(out);
   }
+}
+
+// Vector path: width % 8 == 0, rotary % 16 == 0, 8-element strides and
+// 16-byte aligned pointers. A group of G = next_pow2(width / 8) lanes owns a
+// row, each lane 8 contiguous channels moved as one 16-byte load/store; the
+// normalised partner channels of the RoPE come from the partner lane by a
+// shuffle. Same arithmetic as qk_rms_kernel except the order of the fp32
+// sum of squares.
+struct RmsStrides {
+  int64_t b, s, h;
+};
+
+__global__ void __launch_bounds__(kThreads) qk_rms_vec_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+    const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
+    __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko, const float* __restrict__ cos,
+    const float* __restrict__ sin, uint32_t rows, FastDiv div_heads, FastDiv div_seq, int width,
+    int group, RmsStrides qs, RmsStrides ks, float q_eps, float k_eps, int rotary) {
+  const bool is_key = blockIdx.y == 1;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & (group - 1);
+  const uint32_t row = (blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * (32 / group) + lane / group;
+  const bool live = row < rows;
+  const uint32_t r = live ? row : 0u;
+  const uint32_t bs = fast_div(r, div_heads);
+  const uint32_t h = r - bs * div_heads.d;
+  const uint32_t b = fast_div(bs, div_seq);
+  const uint32_t s = bs - b * div_seq.d;
+  const RmsStrides st = is_key ? ks : qs;
+  const __nv_bfloat16* src = (is_key ? k : q) + b * st.b + s * st.s + h * st.h;
+  const int c0 = sub * 8;
+  const bool has = live && c0 < width;
+  float v[8];
+  unpack_bf16x8(has ? __ldg(reinterpret_cast<const uint4*>(src + c0)) : make_uint4(0, 0, 0, 0), v);
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sq = __fadd_rn(sq, __fmul_rn(v[i], v[i]));
+  for (int o = group / 2; o > 0; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+  const float scale =
+      rsqrtf(__fadd_rn(__fdiv_rn(sq, static_cast<float>(width)), is_key ? k_eps : q_eps));
+  float w[8];
+  unpack_bf16x8(has ? __ldg(reinterpret_cast<const uint4*>((is_key ? kw : qw) + c0)) : make_uint4(0, 0, 0, 0), w);
+  uint32_t nw[4];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2)
+    nw[i / 2] = round_bf16x2(__fmul_rn(__fmul_rn(v[i], scale), w[i]),
+                             __fmul_rn(__fmul_rn(v[i + 1], scale), w[i + 1]));
+  uint4 out = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+  if (rotary > 0) {
+    const int half = rotary / 2;
+    const bool first = c0 < half;
+    const int psub = c0 >= rotary ? sub : (first ? sub + half / 8 : sub - half / 8);
+    const int src_lane = (lane & ~(group - 1)) | psub;
+    uint32_t pw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pw[i] = __shfl_sync(0xffffffffu, nw[i], src_lane);
+    if (has && c0 < rotary)
+      out = rope8_bf16(out, make_uint4(pw[0], pw[1], pw[2], pw[3]), first,
+                       cos + static_cast<int64_t>(s) * rotary + c0, sin + static_cast<int64_t>(s) * rotary + c0);
+  }
+  if (has)
+    *reinterpret_cast<uint4*>((is_key ? ko : qo) + static_cast<int64_t>(row) * width + c0) = out;
 }
 
 // ---------------------------------------------------------------- indexed affine
@@ -240,7 +299,8 @@ XGB_API int xgb_partial_rope(const void* q, const void* k, const float* cos, con
   const int64_t n = batch * seq * heads * width;
   if (n == 0) return XGB_OK;
   const bool vec = width % 8 == 0 && (rotary / 2) % 8 == 0 && aligned16(q) && aligned16(k) &&
-                   aligned16(q_out) && aligned16(k_out) && aligned16(cos) && aligned16(sin);
+                   aligned16(q_out) && aligned16(k_out) && aligned16(cos) && aligned16(sin) &&
+                   n / 8 <= UINT32_MAX && batch * seq <= UINT32_MAX;
   cudaStream_t st = as_stream(stream);
   auto qb = static_cast<const __nv_bfloat16*>(q);
   auto kb = static_cast<const __nv_bfloat16*>(k);
@@ -248,8 +308,10 @@ XGB_API int xgb_partial_rope(const void* q, const void* k, const float* cos, con
   auto ko = static_cast<__nv_bfloat16*>(k_out);
   if (vec) {
     dim3 grid(static_cast<unsigned>(cdiv(n / 8, kThreads)), 2);
-    partial_rope_vec_kernel<<<grid, kThreads, 0, st>>>(qb, kb, cos, sin, qo, ko, n, seq, heads,
-                                                       width, rotary);
+    partial_rope_vec_kernel<<<grid, kThreads, 0, st>>>(
+        qb, kb, cos, sin, qo, ko, static_cast<uint32_t>(n / 8),
+        make_fastdiv(static_cast<uint32_t>(width / 8)), make_fastdiv(static_cast<uint32_t>(heads)),
+        make_fastdiv(static_cast<uint32_t>(seq)), static_cast<int>(rotary));
   } else {
     dim3 grid(static_cast<unsigned>(cdiv(n, kThreads)), 2);
     partial_rope_scalar_kernel<<<grid, kThreads, 0, st>>>(qb, kb, cos, sin, qo, ko, n, seq, heads,
@@ -271,6 +333,25 @@ XGB_API int xgb_qk_rms(const void* q, const int64_t* q_strides, const void* k,
   if (rotary > 0 && (!cos || !sin)) return XGB_ERR_ARG;
   const int64_t rows = batch * seq * heads;
   if (rows == 0) return XGB_OK;
+  bool vec = width % 8 == 0 && rotary % 16 == 0 && rows <= UINT32_MAX && aligned16(q) &&
+             aligned16(k) && aligned16(q_weight) && aligned16(k_weight) && aligned16(q_out) &&
+             aligned16(k_out) && (rotary == 0 || (aligned16(cos) && aligned16(sin)));
+  for (int d = 0; d < 3; ++d) vec = vec && q_strides[d] % 8 == 0 && k_strides[d] % 8 == 0;
+  if (vec) {
+    int group = 1;
+    while (group < width / 8) group <<= 1;
+    const int64_t rows_per_block = (kThreads / 32) * (32 / group);
+    dim3 grid(static_cast<unsigned>(cdiv(rows, rows_per_block)), 2);
+    qk_rms_vec_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(
+        static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+        static_cast<const __nv_bfloat16*>(q_weight), static_cast<const __nv_bfloat16*>(k_weight),
+        static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), cos, sin,
+        static_cast<uint32_t>(rows), make_fastdiv(static_cast<uint32_t>(heads)),
+        make_fastdiv(static_cast<uint32_t>(seq)), static_cast<int>(width), group,
+        RmsStrides{q_strides[0], q_strides[1], q_strides[2]},
+        RmsStrides{k_strides[0], k_strides[1], k_strides[2]}, q_eps, k_eps, static_cast<int>(rotary));
+    return launch_status();
+  }
   dim3 grid(static_cast<unsigned>(cdiv(rows, kThreads / 32)), 2);
   qk_rms_kernel<<<grid, kThreads, 0, as_stream(stream)>>>(
       static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),

@@ -10,7 +10,8 @@
 // caller-provided workspace, as the reference's `peaks` tensor does.
 //
 // Per-token (the B200 FP8 Linear's activation scheme): the same formula per
-// row, computed by one warp per row.
+// row, computed by one CTA per row from registers (rows up to 16,384 wide,
+// vector-aligned) or one warp per row.
 #include <cfloat>
 #include <mutex>
 
@@ -151,6 +152,75 @@ __global__ void __launch_bounds__(kThreads) per_token_kernel(const T* __restrict
   }
 }
 
+// One CTA per row for rows of up to 16,384 channels: the row is read once
+// into registers (P 16-byte chunks per thread), reduced, and packed from the
+// registers, so it crosses HBM once (a warp-per-row pass re-reads rows that
+// no longer fit L2 at FFN widths). Same values as per_token_kernel.
+constexpr int kRowThreads = 256;
+
+template <typename T, int P>
+__global__ void __launch_bounds__(kRowThreads) per_token_row_kernel(
+    const T* __restrict__ x, int64_t cols, int64_t row_stride, uint8_t* __restrict__ out,
+    float* __restrict__ scales) {
+  __shared__ int red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int chunks = static_cast<int>(cols / 8);
+  const uint4* src = reinterpret_cast<const uint4*>(x + row * row_stride);
+  uint4 raw[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const int c = threadIdx.x + j * kRowThreads;
+    raw[j] = c < chunks ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+  }
+  int m = 0;
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const T* v = reinterpret_cast<const T*>(&raw[j]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m = max(m, abs_bits(to_float<T>(v[e])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kRowThreads / 32; ++i) m = max(m, red[i]);
+  const float amax_scale = __fdiv_rn(__int_as_float(m), 448.0f);
+  const float scale = isnan(amax_scale) ? amax_scale : fmaxf(amax_scale, FLT_MIN);
+  if (threadIdx.x == 0) scales[row] = scale;
+  const float y = __frcp_rn(scale);
+  uint2* dst = reinterpret_cast<uint2*>(out + row * cols);
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const int c = threadIdx.x + j * kRowThreads;
+    if (c < chunks) {
+      const T* v = reinterpret_cast<const T*>(&raw[j]);
+      uint32_t q[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2)
+        q[e / 2] = e4m3x2(fminf(fmaxf(div_by(to_float<T>(v[e]), scale, y), -448.f), 448.f),
+                          fminf(fmaxf(div_by(to_float<T>(v[e + 1]), scale, y), -448.f), 448.f));
+      dst[c] = make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
+    }
+  }
+}
+
+template <typename T>
+bool launch_per_token_rows(const T* x, int64_t rows, int64_t cols, int64_t row_stride,
+                           uint8_t* out, float* scales, cudaStream_t st) {
+  const int64_t per_thread = cdiv(cols / 8, kRowThreads);
+  if (cols % 8 || row_stride % 8 || per_thread > 8 || rows > INT32_MAX ||
+      (reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(out) & 7u))
+    return false;
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (per_thread <= 1) per_token_row_kernel<T, 1><<<grid, kRowThreads, 0, st>>>(x, cols, row_stride, out, scales);
+  else if (per_thread <= 2) per_token_row_kernel<T, 2><<<grid, kRowThreads, 0, st>>>(x, cols, row_stride, out, scales);
+  else if (per_thread <= 4) per_token_row_kernel<T, 4><<<grid, kRowThreads, 0, st>>>(x, cols, row_stride, out, scales);
+  else if (per_thread <= 6) per_token_row_kernel<T, 6><<<grid, kRowThreads, 0, st>>>(x, cols, row_stride, out, scales);
+  else per_token_row_kernel<T, 8><<<grid, kRowThreads, 0, st>>>(x, cols, row_stride, out, scales);
+  return true;
+}
+
 }  // namespace
 }  // namespace xgb
 
@@ -230,6 +300,11 @@ XGB_API int xgb_fp8_quantize_per_token(const void* x, int dtype, int64_t rows, i
   if (rows == 0) return XGB_OK;
   const unsigned grid = static_cast<unsigned>(cdiv(rows, kThreads / 32));
   cudaStream_t st = as_stream(stream);
+  const bool by_rows =
+      dtype == XGB_BF16
+          ? launch_per_token_rows(static_cast<const __nv_bfloat16*>(x), rows, cols, row_stride, out, scales, st)
+          : launch_per_token_rows(static_cast<const __half*>(x), rows, cols, row_stride, out, scales, st);
+  if (by_rows) return launch_status();
   if (dtype == XGB_BF16)
     per_token_kernel<<<grid, kThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, cols,
                                                  row_stride, out, scales);

@@ -12,12 +12,136 @@
 // One CTA per row; the row stays in registers between the passes. With no
 // e4m3 output it is the final layer's output AdaLN, norm_out + modulation
 // (x_diffusers/x_diffusers/framework/transformer/minimax_h3.py:672-696).
+//
+// Rows whose width, strides and pointers allow it take the vector kernel:
+// 128 threads, each owning 8-channel chunks moved as 16-byte loads (bf16)
+// and 8-byte stores (e4m3), the modulated row kept as packed bf16 between
+// the amax reduction and the quantisation, and the per-element division by
+// the row scale done as a Markstein-corrected reciprocal multiply (the same
+// correctly rounded quotient as a division). Other layouts take the scalar
+// kernel, which computes the same values.
 #include <cfloat>
+#include <type_traits>
 
 #include "xgb_common.cuh"
 
 namespace xgb {
 namespace {
+
+constexpr int kVecThreads = 128;
+constexpr int kVecMaxChunks = 6;  // 8-channel chunks per thread: width <= 128 * 6 * 8 = 6144
+
+template <bool kMax>
+__device__ __forceinline__ float reduce128(float v, float* red) {
+  v = kMax ? warp_max(v) : warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const float r = kMax ? fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]))
+                       : (red[0] + red[1]) + (red[2] + red[3]);
+  __syncthreads();
+  return r;
+}
+
+// kVecChunks = ceil(width / 1024) chunks per thread, so narrow rows hold
+// fewer registers and more rows are in flight per SM.
+template <bool kRms, int kVecChunks>
+__global__ void __launch_bounds__(kVecThreads) norm_modulate_quant_vec_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, int width, int seq,
+    const __nv_bfloat16* __restrict__ weight, float eps, const __nv_bfloat16* __restrict__ scale,
+    int64_t lds, const __nv_bfloat16* __restrict__ shift, int64_t ldsh,
+    const int64_t* __restrict__ idx, uint8_t* __restrict__ out, float* __restrict__ out_scale,
+    __nv_bfloat16* __restrict__ out_bf16) {
+  __shared__ float red[kVecThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int chunks = width >> 3;
+  const __nv_bfloat16* xr = x + row * ldx;
+  uint4 raw[kVecChunks];
+#pragma unroll
+  for (int j = 0; j < kVecChunks; ++j) {
+    const int c = threadIdx.x + j * kVecThreads;
+    raw[j] = c < chunks ? __ldg(reinterpret_cast<const uint4*>(xr) + c) : make_uint4(0, 0, 0, 0);
+  }
+  const int64_t t = idx[row % seq];
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < kVecChunks; ++j) {
+    float f[8];
+    unpack_bf16x8(raw[j], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc = kRms ? fmaf(f[e], f[e], acc) : acc + f[e];
+  }
+  float mean = 0.f, rstd;
+  if constexpr (kRms) {
+    rstd = rsqrtf(reduce128<false>(acc, red) / width + eps);
+  } else {
+    mean = reduce128<false>(acc, red) / width;
+    float d2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kVecChunks; ++j) {
+      if (threadIdx.x + j * kVecThreads < chunks) {
+        float f[8];
+        unpack_bf16x8(raw[j], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = f[e] - mean;
+          d2 = fmaf(d, d, d2);
+        }
+      }
+    }
+    rstd = rsqrtf(reduce128<false>(d2, red) / width + eps);
+  }
+  float amax = 0.f;
+  const uint4* sc4 = reinterpret_cast<const uint4*>(scale + t * lds);
+  const uint4* sh4 = reinterpret_cast<const uint4*>(shift + t * ldsh);
+#pragma unroll
+  for (int j = 0; j < kVecChunks; ++j) {
+    const int c = threadIdx.x + j * kVecThreads;
+    if (c < chunks) {
+      float f[8], sc[8], sh[8], w[8];
+      unpack_bf16x8(raw[j], f);
+      unpack_bf16x8(__ldg(sc4 + c), sc);
+      unpack_bf16x8(__ldg(sh4 + c), sh);
+      if (kRms && weight) unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(weight) + c), w);
+      uint32_t h2[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float h[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float n = (f[e + u] - mean) * rstd;
+          if (kRms && weight) n *= w[e + u];
+          n = bf16_round(n);
+          const float m = bf16_round(__fadd_rn(1.0f, sc[e + u]));
+          h[u] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(n, m)), sh[e + u]));
+          amax = fmaxf(amax, fabsf(h[u]));
+        }
+        h2[e / 2] = pack_exact_bf16x2(h[0], h[1]);
+      }
+      raw[j] = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+      if (out_bf16) reinterpret_cast<uint4*>(out_bf16 + row * static_cast<int64_t>(width))[c] = raw[j];
+    }
+  }
+  if (!out) return;  // modulation only (the final layer's output AdaLN)
+  amax = reduce128<true>(amax, red);
+  const float s = fmaxf(__fdiv_rn(amax, 448.0f), FLT_MIN);
+  const float y = __frcp_rn(s);
+  if (threadIdx.x == 0) out_scale[row] = s;
+  uint2* orow = reinterpret_cast<uint2*>(out + row * static_cast<int64_t>(width));
+#pragma unroll
+  for (int j = 0; j < kVecChunks; ++j) {
+    const int c = threadIdx.x + j * kVecThreads;
+    if (c < chunks) {
+      float h[8];
+      unpack_bf16x8(raw[j], h);
+      uint32_t q[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2)
+        q[e / 2] = e4m3x2(fminf(fmaxf(div_by(h[e], s, y), -448.f), 448.f),
+                          fminf(fmaxf(div_by(h[e + 1], s, y), -448.f), 448.f));
+      orow[c] = make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
+    }
+  }
+}
 
 constexpr int kThreads = 256;
 constexpr int kMaxPerThread = 24;  // width <= 256 * 24 = 6144
@@ -137,6 +261,28 @@ XGB_API int xgb_norm_modulate_quant(const void* x, int64_t ldx, int64_t rows, in
   auto ob = static_cast<__nv_bfloat16*>(out_bf16);
   cudaStream_t st = as_stream(stream);
   const unsigned grid = static_cast<unsigned>(rows);
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec = width % 8 == 0 && width <= kVecThreads * kVecMaxChunks * 8 && ldx % 8 == 0 &&
+                   lds % 8 == 0 && ldsh % 8 == 0 && a16(x) && a16(scale) && a16(shift) &&
+                   (!weight || a16(weight)) && (!out_bf16 || a16(out_bf16)) &&
+                   (reinterpret_cast<uintptr_t>(out) & 7u) == 0;
+  if (vec) {
+    const int per_thread = static_cast<int>(cdiv(width / 8, kVecThreads));
+    auto run = [&](auto rms, auto chunks) {
+      norm_modulate_quant_vec_kernel<decltype(rms)::value, decltype(chunks)::value>
+          <<<grid, kVecThreads, 0, st>>>(xb, ldx, static_cast<int>(width), static_cast<int>(seq), wb,
+                                         eps, sb, lds, hb, ldsh, indices, out, out_scale, ob);
+    };
+    auto pick = [&](auto rms) {
+      if (per_thread <= 2) run(rms, std::integral_constant<int, 2>{});
+      else if (per_thread <= 3) run(rms, std::integral_constant<int, 3>{});
+      else if (per_thread <= 4) run(rms, std::integral_constant<int, 4>{});
+      else run(rms, std::integral_constant<int, kVecMaxChunks>{});
+    };
+    if (norm_kind == 1) pick(std::true_type{});
+    else pick(std::false_type{});
+    return launch_status();
+  }
   if (norm_kind == 1)
     norm_modulate_quant_kernel<true><<<grid, kThreads, 0, st>>>(
         xb, ldx, static_cast<int>(width), static_cast<int>(seq), wb, eps, sb, lds, hb, ldsh,

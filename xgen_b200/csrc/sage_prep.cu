@@ -57,13 +57,16 @@ inline Workspace carve(void* ws, int64_t bh, int64_t chunks) {
   return w;
 }
 
-// Eight consecutive channels as fp32 from one 16-byte load.
+// Eight consecutive channels of one 16-byte load as fp32.
 template <typename T>
-__device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
-  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+__device__ __forceinline__ void unpack8(const uint4& raw, float (&x)[8]) {
   const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
   for (int j = 0; j < 8; ++j) x[j] = tf<T>(e[j]);
+}
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
+  unpack8<T>(__ldg(reinterpret_cast<const uint4*>(p)), x);
 }
 
 // Per 512-row chunk of one head: channel sums of K and channel abs-max of V.
@@ -163,8 +166,9 @@ __device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, cons
 }
 
 // One CTA per (64-row block, head); thread t owns channels 8*(t%16)..+8 of
-// rows t/16 + 16*i, i < 4 (16-byte loads of 8 channels). Q, K and V are
-// processed one after another so few values are live (several CTAs per SM).
+// rows t/16 + 16*i, i < 4 (16-byte loads of 8 channels). All twelve loads
+// of a thread (Q, K, V) are issued before any is used, kept as raw 16-byte
+// words, and Q, K and V are then quantised one after another.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) quant_kernel(
     const T* __restrict__ q, Strides qs, const T* __restrict__ k, Strides ks,
@@ -182,6 +186,16 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
   const int64_t off0 = (bh * s_pad + row0) * kD + c0;
   __shared__ float red[kThreads / 32];
   float x[4][8];
+  uint4 rq[4], rk[4], rv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = row0 + 16 * i;
+    const bool ok = row < seq;
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    rq[i] = ok ? __ldg(reinterpret_cast<const uint4*>(q + b * qs.b + h * qs.h + row * qs.s + c0)) : zero;
+    rk[i] = ok ? __ldg(reinterpret_cast<const uint4*>(k + b * ks.b + h * ks.h + row * ks.s + c0)) : zero;
+    rv[i] = ok ? __ldg(reinterpret_cast<const uint4*>(v + b * vs.b + h * vs.h + row * vs.s + c0)) : zero;
+  }
 
   // Q: x * sm_scale * log2(e), per-block int8.
   float a = 0.f;
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
   for (int i = 0; i < 4; ++i) {
     const int64_t row = row0 + 16 * i;
     if (row < seq) {
-      load8<T>(q + b * qs.b + h * qs.h + row * qs.s + c0, x[i]);
+      unpack8<T>(rq[i], x[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         x[i][j] = __fmul_rn(x[i][j], q_mult);
@@ -214,7 +228,7 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
   for (int i = 0; i < 4; ++i) {
     const int64_t row = row0 + 16 * i;
     if (row < seq) {
-      load8<T>(k + b * ks.b + h * ks.h + row * ks.s + c0, x[i]);
+      unpack8<T>(rk[i], x[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         x[i][j] = __fsub_rn(x[i][j], mean[j]);
@@ -240,12 +254,7 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t row = row0 + 16 * i;
-    if (row < seq) {
-      load8<T>(v + b * vs.b + h * vs.h + row * vs.s + c0, x[i]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
-    }
+    unpack8<T>(rv[i], x[i]);  // rows >= seq were loaded as zeros
     uint32_t vw[2];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {

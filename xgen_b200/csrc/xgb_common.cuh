@@ -43,6 +43,69 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
   return __half2float(__half(h));
 }
 
+// Two fp32 -> e4m3 bytes (lo in bits 0-7), round-to-nearest-even, saturating.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3));
+}
+
+// Eight bf16 of one 16-byte word as fp32 (exact: bf16 is the top half of fp32).
+__device__ __forceinline__ void unpack_bf16x8(const uint4& raw, float (&f)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Two values that are already bf16 (exactly representable), packed losslessly.
+__device__ __forceinline__ uint32_t pack_exact_bf16x2(float lo, float hi) {
+  return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
+}
+
+// Two fp32 -> packed bf16x2 (lo in bits 0-15), round-to-nearest-even.
+__device__ __forceinline__ uint32_t round_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Packed bf16x2 product, one rounding of the exact product: the same bits as
+// rounding the fp32 product of the two bf16 values (which is exact) to bf16.
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Rotate-half RoPE of 8 bf16 channels that sit on one side of the half
+// split (x_base/x_base/operator/h3_partial_rope.py:9-29): with c = bf16(cos)
+// and s = bf16(sin), out = bf16(bf16(x*c) + bf16(+-partner*s)), the partner
+// negated for the first half. cs/sn point at the 8 fp32 cos/sin entries
+// (16-byte aligned). The products are bf16x2 multiplies, the sum an fp32 add.
+__device__ __forceinline__ uint4 rope8_bf16(const uint4& x, const uint4& partner, bool first,
+                                            const float* cs, const float* sn) {
+  const float4 c_lo = __ldg(reinterpret_cast<const float4*>(cs));
+  const float4 c_hi = __ldg(reinterpret_cast<const float4*>(cs + 4));
+  const float4 s_lo = __ldg(reinterpret_cast<const float4*>(sn));
+  const float4 s_hi = __ldg(reinterpret_cast<const float4*>(sn + 4));
+  const uint32_t neg = first ? 0x80008000u : 0u;
+  const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+  const uint32_t pw[4] = {partner.x ^ neg, partner.y ^ neg, partner.z ^ neg, partner.w ^ neg};
+  const uint32_t cw[4] = {round_bf16x2(c_lo.x, c_lo.y), round_bf16x2(c_lo.z, c_lo.w),
+                          round_bf16x2(c_hi.x, c_hi.y), round_bf16x2(c_hi.z, c_hi.w)};
+  const uint32_t sw[4] = {round_bf16x2(s_lo.x, s_lo.y), round_bf16x2(s_lo.z, s_lo.w),
+                          round_bf16x2(s_hi.x, s_hi.y), round_bf16x2(s_hi.z, s_hi.w)};
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t l = mul_bf16x2(xw[k], cw[k]);
+    const uint32_t r = mul_bf16x2(pw[k], sw[k]);
+    o[k] = round_bf16x2(__fadd_rn(__uint_as_float(l << 16), __uint_as_float(r << 16)),
+                        __fadd_rn(__uint_as_float(l & 0xFFFF0000u), __uint_as_float(r & 0xFFFF0000u)));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // Unsigned division by a divisor fixed for a whole launch, as a multiply-high
 // and shifts (T. Granlund, P. Montgomery, "Division by Invariant Integers
 // using Multiplication", PLDI 1994): with l = ceil(log2 d) and
