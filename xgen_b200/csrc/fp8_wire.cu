@@ -183,7 +183,10 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
 }
 
 // bf16 rows with width % 8 == 0 and (rotary == 0 or rotary % 16 == 0):
-// the same bytes as wire_encode_kernel with fewer instructions. The row
+// the same bytes as wire_encode_kernel with fewer instructions and fewer L2
+// reads. A group of G lanes owns one (peer, seq, batch) position and walks
+// its heads kHeadBlock at a time, so the position's cos/sin are read once
+// for all heads and each lane has kHeadBlock row loads in flight. The row
 // stays packed bf16x2: the RoPE products are bf16x2 multiplies (one
 // rounding of the exact product, as rounding the fp32 product), the sum is
 // an fp32 add rounded once to bf16, the row scale's division by 448 and the
@@ -191,58 +194,75 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
 // correctly rounded quotient; below 448e-12 the 1e-12 floor decides), and
 // the saturating e4m3x2 conversion replaces the clamp to +-448 (values
 // beyond 448 round to 448 either way).
+constexpr int kHeadBlock = 4;
+
 __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a, int group) {
   const int slot = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int sub = lane & (group - 1);
-  const int rows_per_warp = 32 / group;
-  const int64_t row = (static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5)) *
-                          rows_per_warp + lane / group;
-  const bool live = row < a.rows;
-  uint32_t peer, s, bat, head;
-  split_row(live ? static_cast<uint32_t>(row) : 0u, a.div_heads, a.div_batch, a.div_seq, peer, s,
-            bat, head);
+  const int64_t positions = a.rows / a.heads;
+  const int64_t pos = (static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5)) *
+                          (32 / group) + lane / group;
+  const bool live = pos < positions;
+  const uint32_t pr = live ? static_cast<uint32_t>(pos) : 0u;
+  const uint32_t q2 = fast_div(pr, a.div_batch);  // peer * seq + s
+  const uint32_t bat = pr - q2 * a.div_batch.d;
+  const uint32_t peer = fast_div(q2, a.div_seq);
+  const uint32_t s = q2 - peer * a.div_seq.d;
   const int c0 = sub * 8;
   const bool has = live && c0 < a.width && static_cast<int64_t>(peer) * a.seq + s < a.valid_seq;
-  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(a.src[slot]) + peer * a.st[slot][0] +
-                             s * a.st[slot][1] + bat * a.st[slot][2] + head * a.st[slot][3];
-  uint4 raw = has ? __ldg(reinterpret_cast<const uint4*>(src + c0)) : make_uint4(0, 0, 0, 0);
-  if (has && slot < 2 && c0 < a.rotary) {
-    // Fused pre-A2A RoPE (h3_partial_rope.py:9-29): x*cos + rotate_half(x)*sin
-    // with each product and the sum rounded to bf16.
-    const int64_t half = a.rotary / 2;
-    const bool first = c0 < half;
-    const uint4 pr = __ldg(reinterpret_cast<const uint4*>(src + (first ? c0 + half : c0 - half)));
-    raw = rope8_bf16(raw, pr, first, a.cos + static_cast<int64_t>(s) * a.rotary + c0,
-                     a.sin + static_cast<int64_t>(s) * a.rotary + c0);
-  }
-  float x[8];
-  unpack_bf16x8(raw, x);
-  float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fabsf(x[2]));
-  m = fmaxf(fmaxf(m, fabsf(x[3])), fabsf(x[4]));
-  m = fmaxf(fmaxf(m, fabsf(x[5])), fmaxf(fabsf(x[6]), fabsf(x[7])));
-  for (int o = group / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const bool rope = has && slot < 2 && c0 < a.rotary;
+  const int64_t half = a.rotary / 2;
+  const bool first = c0 < half;
+  uint32_t cw[4] = {0, 0, 0, 0}, sw[4] = {0, 0, 0, 0};
+  if (rope)
+    load_cos_sin8(a.cos + static_cast<int64_t>(s) * a.rotary + c0, a.sin + static_cast<int64_t>(s) * a.rotary + c0,
+                  cw, sw);
+  const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(a.src[slot]) + peer * a.st[slot][0] +
+                              s * a.st[slot][1] + bat * a.st[slot][2];
+  const int64_t pofs = first ? half : -half;
   constexpr float kRcp448 = 1.0f / 448.0f;  // RN(1/448)
-  const float scale = fmaxf(div_by(m, 448.0f, kRcp448), 1.0e-12f);
-  if (!live) return;
-
-  const int64_t wire_row = row + (static_cast<int64_t>(peer) * (a.streams - 1) + slot) * a.peer_rows;
-  uint8_t* dst = a.payload + wire_row * (a.width + 4) + static_cast<int64_t>(peer) * a.peer_padding;
-  if (c0 < a.width) {
-    const float y = __frcp_rn(scale);
-    const uint32_t q0 = e4m3x2(div_by(x[0], scale, y), div_by(x[1], scale, y));
-    const uint32_t q1 = e4m3x2(div_by(x[2], scale, y), div_by(x[3], scale, y));
-    const uint32_t q2 = e4m3x2(div_by(x[4], scale, y), div_by(x[5], scale, y));
-    const uint32_t q3 = e4m3x2(div_by(x[6], scale, y), div_by(x[7], scale, y));
-    // Rows start at 4-byte multiples (width % 4 == 0), so two u32 stores.
-    reinterpret_cast<uint32_t*>(dst + c0)[0] = q0 | (q1 << 16);
-    reinterpret_cast<uint32_t*>(dst + c0)[1] = q2 | (q3 << 16);
-  }
-  if (sub == 0) *reinterpret_cast<float*>(dst + a.width) = scale;
-  if (a.peer_padding && sub == 0 && slot == 0 && row % a.peer_rows == 0) {
-    const int64_t packet = a.peer_rows * a.streams * (a.width + 4);
-    uint8_t* tail = a.payload + static_cast<int64_t>(peer) * (packet + a.peer_padding) + packet;
-    for (int64_t i = 0; i < a.peer_padding; ++i) tail[i] = 0;
+  const int64_t wire_base = (static_cast<int64_t>(peer) * (a.streams - 1) + slot) * a.peer_rows;
+  for (int64_t h0 = 0; h0 < a.heads; h0 += kHeadBlock) {
+    uint4 raw[kHeadBlock], par[kHeadBlock];
+#pragma unroll
+    for (int j = 0; j < kHeadBlock; ++j) {
+      const bool hj = has && h0 + j < a.heads;
+      const __nv_bfloat16* src = base + (h0 + j) * a.st[slot][3] + c0;
+      raw[j] = hj ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0, 0, 0, 0);
+      par[j] = hj && rope ? __ldg(reinterpret_cast<const uint4*>(src + pofs)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < kHeadBlock; ++j) {
+      if (h0 + j >= a.heads) break;  // uniform across the warp
+      if (rope) raw[j] = rope8_bf16(raw[j], par[j], first, cw, sw);
+      float x[8];
+      unpack_bf16x8(raw[j], x);
+      float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fabsf(x[2]));
+      m = fmaxf(fmaxf(m, fabsf(x[3])), fabsf(x[4]));
+      m = fmaxf(fmaxf(m, fabsf(x[5])), fmaxf(fabsf(x[6]), fabsf(x[7])));
+      for (int o = group / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float scale = fmaxf(div_by(m, 448.0f, kRcp448), 1.0e-12f);
+      if (!live) continue;
+      const int64_t row = pos * a.heads + h0 + j;
+      uint8_t* dst = a.payload + (row + wire_base) * (a.width + 4) + static_cast<int64_t>(peer) * a.peer_padding;
+      if (c0 < a.width) {
+        const float y = __frcp_rn(scale);
+        const uint32_t e0 = e4m3x2(div_by(x[0], scale, y), div_by(x[1], scale, y));
+        const uint32_t e1 = e4m3x2(div_by(x[2], scale, y), div_by(x[3], scale, y));
+        const uint32_t e2 = e4m3x2(div_by(x[4], scale, y), div_by(x[5], scale, y));
+        const uint32_t e3 = e4m3x2(div_by(x[6], scale, y), div_by(x[7], scale, y));
+        // Rows start at 4-byte multiples (width % 4 == 0), so two u32 stores.
+        reinterpret_cast<uint32_t*>(dst + c0)[0] = e0 | (e1 << 16);
+        reinterpret_cast<uint32_t*>(dst + c0)[1] = e2 | (e3 << 16);
+      }
+      if (sub == 0) *reinterpret_cast<float*>(dst + a.width) = scale;
+      if (a.peer_padding && sub == 0 && slot == 0 && row % a.peer_rows == 0) {
+        const int64_t packet = a.peer_rows * a.streams * (a.width + 4);
+        uint8_t* tail = a.payload + static_cast<int64_t>(peer) * (packet + a.peer_padding) + packet;
+        for (int64_t i = 0; i < a.peer_padding; ++i) tail[i] = 0;
+      }
+    }
   }
 }
 
@@ -359,7 +379,10 @@ XGB_API int xgb_fp8_wire_encode_view(const void* const* sources, const int64_t* 
   dim3 grid(static_cast<unsigned>(cdiv(a.rows, rows_per_block)), streams);
   cudaStream_t st = as_stream(stream);
   if (dtype == XGB_BF16) {
-    if (vec && rotary % 16 == 0) wire_encode_bf16_kernel<<<grid, kThreads, 0, st>>>(a, group);
+    if (vec && rotary % 16 == 0) {
+      const dim3 pgrid(static_cast<unsigned>(cdiv(a.rows / heads, rows_per_block)), streams);
+      wire_encode_bf16_kernel<<<pgrid, kThreads, 0, st>>>(a, group);
+    }
     else if (vec) wire_encode_kernel<__nv_bfloat16, true><<<grid, kThreads, 0, st>>>(a, group);
     else wire_encode_kernel<__nv_bfloat16, false><<<grid, kThreads, 0, st>>>(a, group);
   } else {

@@ -21,8 +21,10 @@
 // of 128 bytes:
 //   warp 0     TMA producer (A 16 KB + W 32 KB per stage, 4 stages)
 //   warp 1     TMEM allocator + MMA issuer (4 x M128 N256 K32 per stage)
-//   warps 2-5  epilogue: one thread per output row (TMEM lane), 256 fp32
-//              columns read in chunks of 32
+//   warps 2-9  epilogue: one thread per output row (TMEM lane) and column
+//              half (warps 2-5 columns 0-127, warps 6-9 columns 128-255),
+//              fp32 read in chunks of 32 columns; per-column scales, bias,
+//              AdaLN gate and residual move as 16-byte vectors
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile run
 // under the MMAs of the next. Every mbarrier wait is bounded.
 #include "sm100.cuh"
@@ -37,7 +39,8 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 128;  // bytes of K per stage (e4m3)
 constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpiThreads = 256;
 constexpr int kABytes = kBM * kBK;
 constexpr int kBBytes = kBN * kBK;
 constexpr int kStageBytes = kABytes + kBBytes;
@@ -75,6 +78,7 @@ struct Params {
   const __nv_bfloat16* residual;
   int64_t ldr;
   int* err;
+  bool vec;  // 16-byte aligned scale/bias/gate/residual columns (host-checked)
 };
 
 struct Barriers {
@@ -108,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bars->acc_full[a], 1);
-      mbar_init(&bars->acc_empty[a], 128);
+      mbar_init(&bars->acc_empty[a], kEpiThreads);
     }
     mbar_init(&bars->end, 1);
     fence_barrier_init();
@@ -177,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;       // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // column half of the tile
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     int lt = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
@@ -194,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // N % 256 == 0 (checked on the host): gate columns n0 + [0, 128),
         // value columns n0 + [128, 256), outputs n0/2 + [0, 128).
 #pragma unroll 1
-        for (int c = 0; c < kBN / 64; ++c) {
+        for (int c = half * (kBN / 128); c < (half + 1) * (kBN / 128); ++c) {
           uint32_t rg[32], rv[32];
           tmem_ld32(lane_addr + a * kBN + c * 32, rg);
           tmem_ld32(lane_addr + a * kBN + kBN / 2 + c * 32, rv);
@@ -225,12 +230,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
         uint32_t r[32];
         tmem_ld32(lane_addr + a * kBN + c * 32, r);
         tmem_ld_wait();
         const int nb = n0 + c * 32;
-        if (row_ok && nb < p.N) {
+        if (row_ok && p.vec && nb + 32 <= p.N) {
+          // 8 columns at a time: scales, bias, gate row and residual as vectors
+          __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
+#pragma unroll
+          for (int g8 = 0; g8 < 4; ++g8) {
+            const int n = nb + g8 * 8;
+            float alpha[8], bias[8], y[8];
+            if (p.sb_stride) {
+              const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.sb + n));
+              const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.sb + n + 4));
+              alpha[0] = sa * b0.x; alpha[1] = sa * b0.y; alpha[2] = sa * b0.z; alpha[3] = sa * b0.w;
+              alpha[4] = sa * b1.x; alpha[5] = sa * b1.y; alpha[6] = sa * b1.z; alpha[7] = sa * b1.w;
+            } else {
+              const float al = sa * p.sb[0];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) alpha[i] = al;
+            }
+            if (p.bias) {
+              unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.bias + n)), bias);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) bias[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              y[i] = fmaf(__uint_as_float(r[g8 * 8 + i]), alpha[i], bias[i]);
+              if constexpr (kEpi == kGeluErf) y[i] = gelu_erf(y[i]);
+              if constexpr (kEpi == kGeluTanh) y[i] = gelu_tanh(y[i]);
+            }
+            if constexpr (kEpi == kGated) {
+              // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
+              float gt[8], res[8];
+              unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.ldg + n)), gt);
+              unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(m) * p.ldr + n)), res);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[i]), gt[i])), res[i]);
+            }
+            reinterpret_cast<uint4*>(dst)[g8] =
+                make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                           pack_bf16x2(y[6], y[7]));
+          }
+        } else if (row_ok && nb < p.N) {
           uint32_t w[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
@@ -350,6 +396,9 @@ XGB_API int xgb_fp8_gemm(const uint8_t* a, const uint8_t* w, int64_t M, int64_t 
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.ldr = ldr;
   p.err = error_flag;
+  const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  p.vec = (scale_w_stride == 0 || a16(scale_w)) && (!bias || a16(bias)) &&
+          (!gated || (a16(gate) && a16(residual) && ldg % 8 == 0 && ldr % 8 == 0));
   cudaStream_t st = as_stream(stream);
   if (gated) return gemm::launch<gemm::kGated>(a, w, p, st);
   if (activation == 1) return gemm::launch<gemm::kGeluErf>(a, w, p, st);

@@ -90,37 +90,40 @@ __global__ void __launch_bounds__(kVecThreads) norm_modulate_quant_vec_kernel(
     }
     rstd = rsqrtf(reduce128<false>(d2, red) / width + eps);
   }
-  float amax = 0.f;
+  // Modulation on packed bf16x2: m = bf16(1 + scale), h = bf16(bf16(n*m) + shift).
+  // With bf16 operands the product is exact in fp32 and the sum is exact in
+  // fp32 unless the smaller operand is below 2^-15 of the larger (then both
+  // roundings return the larger), so the single-rounding bf16x2 operations
+  // give the bits of the fp32 operation rounded to bf16.
+  uint32_t amax2 = 0;  // bf16x2 max of |h|
   const uint4* sc4 = reinterpret_cast<const uint4*>(scale + t * lds);
   const uint4* sh4 = reinterpret_cast<const uint4*>(shift + t * ldsh);
 #pragma unroll
   for (int j = 0; j < kVecChunks; ++j) {
     const int c = threadIdx.x + j * kVecThreads;
     if (c < chunks) {
-      float f[8], sc[8], sh[8], w[8];
+      float f[8], w[8];
       unpack_bf16x8(raw[j], f);
-      unpack_bf16x8(__ldg(sc4 + c), sc);
-      unpack_bf16x8(__ldg(sh4 + c), sh);
+      const uint4 sc = __ldg(sc4 + c), sh = __ldg(sh4 + c);
       if (kRms && weight) unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(weight) + c), w);
+      const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w}, shw[4] = {sh.x, sh.y, sh.z, sh.w};
       uint32_t h2[4];
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        float h[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          float n = (f[e + u] - mean) * rstd;
-          if (kRms && weight) n *= w[e + u];
-          n = bf16_round(n);
-          const float m = bf16_round(__fadd_rn(1.0f, sc[e + u]));
-          h[u] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(n, m)), sh[e + u]));
-          amax = fmaxf(amax, fabsf(h[u]));
+      for (int k = 0; k < 4; ++k) {
+        float n0 = (f[2 * k] - mean) * rstd, n1 = (f[2 * k + 1] - mean) * rstd;
+        if (kRms && weight) {
+          n0 *= w[2 * k];
+          n1 *= w[2 * k + 1];
         }
-        h2[e / 2] = pack_exact_bf16x2(h[0], h[1]);
+        const uint32_t m2 = add_bf16x2(0x3F803F80u /* (1, 1) */, scw[k]);
+        h2[k] = add_bf16x2(mul_bf16x2(round_bf16x2(n0, n1), m2), shw[k]);
+        amax2 = max_bf16x2(amax2, h2[k] & 0x7FFF7FFFu);
       }
       raw[j] = make_uint4(h2[0], h2[1], h2[2], h2[3]);
       if (out_bf16) reinterpret_cast<uint4*>(out_bf16 + row * static_cast<int64_t>(width))[c] = raw[j];
     }
   }
+  float amax = fmaxf(__uint_as_float(amax2 << 16), __uint_as_float(amax2 & 0xFFFF0000u));
   if (!out) return;  // modulation only (the final layer's output AdaLN)
   amax = reduce128<true>(amax, red);
   const float s = fmaxf(__fdiv_rn(amax, 448.0f), FLT_MIN);

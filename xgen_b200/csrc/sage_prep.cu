@@ -133,23 +133,25 @@ __global__ void __launch_bounds__(kD) finalize_kernel(Workspace w, int64_t chunk
   v_scale[bh * kD + c] = fmaxf(s, FLT_MIN);
 }
 
-// Block abs-max over the CTA (256 threads).
+// Block abs-max over the CTA (kN threads).
+template <int kN>
 __device__ __forceinline__ float block_absmax(float a, float* red) {
   a = warp_max(a);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
   __syncthreads();
   float r = 0.f;
 #pragma unroll
-  for (int i = 0; i < kThreads / 32; ++i) r = fmaxf(r, red[i]);
+  for (int i = 0; i < kN / 32; ++i) r = fmaxf(r, red[i]);
   __syncthreads();
   return r;
 }
 
-// 4 rows x 8 channels of int8 codes round(x / s) clamped to +-127.
-__device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, const float (&x)[4][8],
+// R rows (64 / R apart) x 8 channels of int8 codes round(x / s) clamped to +-127.
+template <int R>
+__device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, const float (&x)[R][8],
                                            float s, float y) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < R; ++i) {
     uint32_t w[2];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -161,16 +163,19 @@ __device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, cons
       }
       w[half] = word;
     }
-    *reinterpret_cast<uint2*>(dst + 16 * i * row_stride) = make_uint2(w[0], w[1]);
+    *reinterpret_cast<uint2*>(dst + (64 / R) * i * row_stride) = make_uint2(w[0], w[1]);
   }
 }
 
-// One CTA per (64-row block, head); thread t owns channels 8*(t%16)..+8 of
-// rows t/16 + 16*i, i < 4 (16-byte loads of 8 channels). All twelve loads
-// of a thread (Q, K, V) are issued before any is used, kept as raw 16-byte
-// words, and Q, K and V are then quantised one after another.
+// One CTA of 512 threads per (64-row block, head); thread t owns channels
+// 8*(t%16)..+8 of rows t/16 + 32*i, i < 2 (16-byte loads of 8 channels).
+// All six loads of a thread (Q, K, V) are issued before any is used, kept as
+// raw 16-byte words, and Q, K and V are then quantised one after another.
+constexpr int kQuantThreads = 512;
+constexpr int kQuantRows = 64 * 16 / kQuantThreads;  // rows per thread
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads) quant_kernel(
+__global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
     const T* __restrict__ q, Strides qs, const T* __restrict__ k, Strides ks,
     const T* __restrict__ v, Strides vs, int64_t heads, int64_t seq, int64_t s_pad,
     float q_mult, Workspace w, const float* __restrict__ v_scale, int8_t* __restrict__ q8,
@@ -184,12 +189,14 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
   const int c0 = cg * 8;
   const int64_t row0 = blk * 64 + rr;
   const int64_t off0 = (bh * s_pad + row0) * kD + c0;
-  __shared__ float red[kThreads / 32];
-  float x[4][8];
-  uint4 rq[4], rk[4], rv[4];
+  constexpr int R = kQuantRows;
+  constexpr int kStep = 64 / R;
+  __shared__ float red[kQuantThreads / 32];
+  float x[R][8];
+  uint4 rq[R], rk[R], rv[R];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t row = row0 + 16 * i;
+  for (int i = 0; i < R; ++i) {
+    const int64_t row = row0 + kStep * i;
     const bool ok = row < seq;
     const uint4 zero = make_uint4(0, 0, 0, 0);
     rq[i] = ok ? __ldg(reinterpret_cast<const uint4*>(q + b * qs.b + h * qs.h + row * qs.s + c0)) : zero;
@@ -197,26 +204,29 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
     rv[i] = ok ? __ldg(reinterpret_cast<const uint4*>(v + b * vs.b + h * vs.h + row * vs.s + c0)) : zero;
   }
 
+  // Values are recomputed from the raw words in each pass (the same
+  // operations give the same bits), which keeps few registers live.
+  bool ok[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) ok[i] = row0 + kStep * i < seq;
+
   // Q: x * sm_scale * log2(e), per-block int8.
   float a = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t row = row0 + 16 * i;
-    if (row < seq) {
-      unpack8<T>(rq[i], x[i]);
+  for (int i = 0; i < R; ++i) {
+    unpack8<T>(rq[i], x[i]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        x[i][j] = __fmul_rn(x[i][j], q_mult);
-        a = fmaxf(a, fabsf(x[i][j]));
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
-    }
+    for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(__fmul_rn(x[i][j], q_mult)));
   }
-  a = block_absmax(a, red);
+  a = block_absmax<kQuantThreads>(a, red);
   float sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
   if (threadIdx.x == 0) q_scale[bh * (s_pad / 64) + blk] = sc;
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    unpack8<T>(rq[i], x[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[i][j] = __fmul_rn(x[i][j], q_mult);  // rows >= seq: 0
+  }
   store_int8(q8 + off0, kD, x, sc, __frcp_rn(sc));
 
   // K: x - mean over the sequence, per-block int8.
@@ -225,26 +235,23 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
   for (int j = 0; j < 8; ++j) mean[j] = w.kmean[bh * kD + c0 + j];
   a = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t row = row0 + 16 * i;
-    if (row < seq) {
-      unpack8<T>(rk[i], x[i]);
+  for (int i = 0; i < R; ++i) {
+    unpack8<T>(rk[i], x[i]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        x[i][j] = __fsub_rn(x[i][j], mean[j]);
-        a = fmaxf(a, fabsf(x[i][j]));
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
-    }
+    for (int j = 0; j < 8; ++j) a = fmaxf(a, ok[i] ? fabsf(__fsub_rn(x[i][j], mean[j])) : 0.f);
   }
-  a = block_absmax(a, red);
+  a = block_absmax<kQuantThreads>(a, red);
   sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
   if (threadIdx.x == 0) k_scale[bh * (s_pad / 64) + blk] = sc;
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    unpack8<T>(rk[i], x[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[i][j] = ok[i] ? __fsub_rn(x[i][j], mean[j]) : 0.f;
+  }
   store_int8(k8 + off0, kD, x, sc, __frcp_rn(sc));
 
-  // V: per-channel e4m3.
+  // V: per-channel e4m3 (rows >= seq were loaded as zeros).
   float vsc[8], vrc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -252,21 +259,13 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(
     vrc[j] = __frcp_rn(vsc[j]);
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t row = row0 + 16 * i;
-    unpack8<T>(rv[i], x[i]);  // rows >= seq were loaded as zeros
-    uint32_t vw[2];
+  for (int i = 0; i < R; ++i) {
+    unpack8<T>(rv[i], x[i]);
+    uint32_t q[4];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int jj = half * 4 + j;
-        word |= static_cast<uint32_t>(f32_to_e4m3(div_by(x[i][jj], vsc[jj], vrc[jj]))) << (8 * j);
-      }
-      vw[half] = word;
-    }
-    *reinterpret_cast<uint2*>(v8 + off0 + 16 * i * kD) = make_uint2(vw[0], vw[1]);
+    for (int j = 0; j < 8; j += 2)
+      q[j / 2] = e4m3x2(div_by(x[i][j], vsc[j], vrc[j]), div_by(x[i][j + 1], vsc[j + 1], vrc[j + 1]));
+    *reinterpret_cast<uint2*>(v8 + off0 + kStep * i * kD) = make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
   }
 }
 
@@ -323,7 +322,7 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
     auto vb = static_cast<const __nv_bfloat16*>(v);
     stats_kernel<<<sgrid, kThreads, 0, st>>>(kb, ks, vb, vs, heads, seq, w, chunks);
     finalize_kernel<<<static_cast<unsigned>(bh), kD, 0, st>>>(w, chunks, seq, v_scale);
-    quant_kernel<<<qgrid, kThreads, 0, st>>>(qb, qs, kb, ks, vb, vs, heads, seq, s_pad, q_mult,
+    quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(qb, qs, kb, ks, vb, vs, heads, seq, s_pad, q_mult,
                                               w, v_scale, q8, q_scale, k8, k_scale, v8);
   } else {
     auto qh = static_cast<const __half*>(q);
@@ -331,7 +330,7 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
     auto vh = static_cast<const __half*>(v);
     stats_kernel<<<sgrid, kThreads, 0, st>>>(kh, ks, vh, vs, heads, seq, w, chunks);
     finalize_kernel<<<static_cast<unsigned>(bh), kD, 0, st>>>(w, chunks, seq, v_scale);
-    quant_kernel<<<qgrid, kThreads, 0, st>>>(qh, qs, kh, ks, vh, vs, heads, seq, s_pad, q_mult,
+    quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(qh, qs, kh, ks, vh, vs, heads, seq, s_pad, q_mult,
                                               w, v_scale, q8, q_scale, k8, k_scale, v8);
   }
   return launch_status();

@@ -77,33 +77,59 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   return d;
 }
 
+// Packed bf16x2 sum, one rounding of the exact sum.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Packed bf16x2 maximum (a NaN operand yields the other operand, as fmaxf).
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // Rotate-half RoPE of 8 bf16 channels that sit on one side of the half
 // split (x_base/x_base/operator/h3_partial_rope.py:9-29): with c = bf16(cos)
 // and s = bf16(sin), out = bf16(bf16(x*c) + bf16(+-partner*s)), the partner
-// negated for the first half. cs/sn point at the 8 fp32 cos/sin entries
-// (16-byte aligned). The products are bf16x2 multiplies, the sum an fp32 add.
-__device__ __forceinline__ uint4 rope8_bf16(const uint4& x, const uint4& partner, bool first,
-                                            const float* cs, const float* sn) {
+// negated for the first half. The products and the sum are bf16x2
+// operations: the product of two bf16 values is exact in fp32, and so is the
+// sum of two bf16 values unless the smaller is below 2^-15 of the larger
+// (then rounding the fp32 sum and rounding the exact sum both return the
+// larger), so one rounding of the exact result gives the bits of the fp32
+// operation rounded to bf16. cw/sw hold c and s as packed bf16x2.
+__device__ __forceinline__ void load_cos_sin8(const float* cs, const float* sn, uint32_t (&cw)[4],
+                                              uint32_t (&sw)[4]) {
   const float4 c_lo = __ldg(reinterpret_cast<const float4*>(cs));
   const float4 c_hi = __ldg(reinterpret_cast<const float4*>(cs + 4));
   const float4 s_lo = __ldg(reinterpret_cast<const float4*>(sn));
   const float4 s_hi = __ldg(reinterpret_cast<const float4*>(sn + 4));
+  cw[0] = round_bf16x2(c_lo.x, c_lo.y); cw[1] = round_bf16x2(c_lo.z, c_lo.w);
+  cw[2] = round_bf16x2(c_hi.x, c_hi.y); cw[3] = round_bf16x2(c_hi.z, c_hi.w);
+  sw[0] = round_bf16x2(s_lo.x, s_lo.y); sw[1] = round_bf16x2(s_lo.z, s_lo.w);
+  sw[2] = round_bf16x2(s_hi.x, s_hi.y); sw[3] = round_bf16x2(s_hi.z, s_hi.w);
+}
+
+__device__ __forceinline__ uint4 rope8_bf16(const uint4& x, const uint4& partner, bool first,
+                                            const uint32_t (&cw)[4], const uint32_t (&sw)[4]) {
   const uint32_t neg = first ? 0x80008000u : 0u;
   const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
   const uint32_t pw[4] = {partner.x ^ neg, partner.y ^ neg, partner.z ^ neg, partner.w ^ neg};
-  const uint32_t cw[4] = {round_bf16x2(c_lo.x, c_lo.y), round_bf16x2(c_lo.z, c_lo.w),
-                          round_bf16x2(c_hi.x, c_hi.y), round_bf16x2(c_hi.z, c_hi.w)};
-  const uint32_t sw[4] = {round_bf16x2(s_lo.x, s_lo.y), round_bf16x2(s_lo.z, s_lo.w),
-                          round_bf16x2(s_hi.x, s_hi.y), round_bf16x2(s_hi.z, s_hi.w)};
   uint32_t o[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t l = mul_bf16x2(xw[k], cw[k]);
-    const uint32_t r = mul_bf16x2(pw[k], sw[k]);
-    o[k] = round_bf16x2(__fadd_rn(__uint_as_float(l << 16), __uint_as_float(r << 16)),
-                        __fadd_rn(__uint_as_float(l & 0xFFFF0000u), __uint_as_float(r & 0xFFFF0000u)));
-  }
+  for (int k = 0; k < 4; ++k)
+    o[k] = add_bf16x2(mul_bf16x2(xw[k], cw[k]), mul_bf16x2(pw[k], sw[k]));
   return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// The same with cos/sin read from the 8 fp32 entries at cs/sn (16-byte aligned).
+__device__ __forceinline__ uint4 rope8_bf16(const uint4& x, const uint4& partner, bool first,
+                                            const float* cs, const float* sn) {
+  uint32_t cw[4], sw[4];
+  load_cos_sin8(cs, sn, cw, sw);
+  return rope8_bf16(x, partner, first, cw, sw);
 }
 
 // Unsigned division by a divisor fixed for a whole launch, as a multiply-high
