@@ -165,3 +165,58 @@ def test_per_token_quant_vs_oracle(cuda_device):
     rc, rs = of.quantize_per_token(x.float().numpy())
     assert np.array_equal(scales.cpu().numpy(), rs)
     assert np.array_equal(codes.view(torch.uint8).cpu().numpy(), rc)
+
+
+@pytest.mark.parametrize("rows,cols", [(97, 12288), (64, 100), (5, 16384)])
+def test_per_token_quant_widths_vs_oracle(cuda_device, rows, cols):
+    """The CTA-per-row kernel (rows up to 16,384 wide, 1-8 chunks per thread)
+    and the warp-per-row fallback (unaligned widths) against the oracle."""
+    from xgen_b200.ops import quantize_per_token
+
+    g = torch.Generator().manual_seed(rows + cols)
+    x = (torch.randn(rows, cols, generator=g) * torch.rand(rows, 1, generator=g) * 10).bfloat16()
+    codes, scales = quantize_per_token(x.to(cuda_device))
+    rc, rs = of.quantize_per_token(x.float().numpy())
+    assert np.array_equal(scales.cpu().numpy(), rs)
+    assert np.array_equal(codes.view(torch.uint8).cpu().numpy(), rc)
+
+
+@pytest.mark.parametrize("peers,seq,batch,hpd,rotary,valid", [
+    (2, 40, 1, 3, 128, None),   # 16 channels per lane, full rotary
+    (4, 33, 2, 2, 96, 120),     # 16 channels per lane, partial rotary, masked tail
+    (1, 50, 1, 5, 48, None),    # 8 channels per lane
+    (2, 21, 1, 3, 40, 37),      # generic kernel (rotary half not a multiple of 8)
+])
+def test_wire_encode_fused_rope_vs_oracle(cuda_device, peers, seq, batch, hpd, rotary, valid):
+    """PHAA FP8 wire encode with the pre-A2A RoPE fused in, on the
+    [peer, seq, batch, head] views PHAA passes, bit-exact against the
+    oracle's RoPE (h3_partial_rope.py:9-29) followed by its wire encode
+    (fp8_transport.py:26-63); rows at global sequence index >= valid encode
+    as zeros."""
+    from xgen_b200.phaa import fp8_transport as fp8
+    from xgen_b200.phaa.fp8_transport import WireView
+
+    heads = peers * hpd
+    g = torch.Generator().manual_seed(seq * 7 + rotary)
+    q, k, v = (torch.randn(batch, seq, heads * 128, generator=g).bfloat16() for _ in range(3))
+    ang = torch.rand(seq, rotary // 2, generator=g) * 6.0
+    cos = torch.cat([ang.cos(), ang.cos()], dim=-1).float()
+    sin = torch.cat([ang.sin(), ang.sin()], dim=-1).float()
+    views = [t.to(cuda_device).unflatten(-1, (heads, 128)).unflatten(2, (peers, hpd)).permute(2, 1, 0, 3, 4)
+             for t in (q, k, v)]
+    got = fp8.encode([x for x in views], 128, peers, rotary_emb=(cos.to(cuda_device), sin.to(cuda_device)),
+                     views=[WireView.of(x) for x in views], valid_seq=valid)
+    # oracle: RoPE on [B, S, H, D], the same views, masked rows zeroed, encode
+    q4, k4, v4 = (t.float().numpy().reshape(batch, seq, heads, 128) for t in (q, k, v))
+    qr, kr = ew.partial_rope(q4, k4, cos.numpy(), sin.numpy())
+    srcs = []
+    for x in (qr, kr, v4):
+        x5 = x.reshape(batch, seq, peers, hpd, 128).transpose(2, 1, 0, 3, 4).copy()
+        if valid is not None:
+            for p in range(peers):
+                for s in range(seq):
+                    if p * seq + s >= valid:
+                        x5[p, s] = 0
+        srcs.append(x5)
+    want = of.wire_encode(srcs, peers)
+    assert np.array_equal(got.cpu().numpy(), want)

@@ -182,20 +182,21 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
   }
 }
 
-// bf16 rows with width % 8 == 0 and (rotary == 0 or rotary % 16 == 0):
+// bf16 rows with width % (8V) == 0 and (rotary == 0 or rotary % (16V) == 0):
 // the same bytes as wire_encode_kernel with fewer instructions and fewer L2
 // reads. A group of G lanes owns one (peer, seq, batch) position and walks
-// its heads kHeadBlock at a time, so the position's cos/sin are read once
-// for all heads and each lane has kHeadBlock row loads in flight. The row
-// stays packed bf16x2: the RoPE products are bf16x2 multiplies (one
-// rounding of the exact product, as rounding the fp32 product), the sum is
-// an fp32 add rounded once to bf16, the row scale's division by 448 and the
-// per-element x / scale are Markstein-corrected reciprocal multiplies (the
-// correctly rounded quotient; below 448e-12 the 1e-12 floor decides), and
-// the saturating e4m3x2 conversion replaces the clamp to +-448 (values
+// its heads kHeadBlock at a time, each lane 8V channels (V 16-byte words),
+// so the position's cos/sin are read once for all heads, the per-row index
+// and scale work is shared by 8V channels, and each lane has several row
+// loads in flight. The row stays packed bf16x2: the RoPE products and sum
+// are bf16x2 operations (rope8_bf16), the row scale's division by 448 and
+// the per-element x / scale are Markstein-corrected reciprocal multiplies
+// (the correctly rounded quotient; below 448e-12 the 1e-12 floor decides),
+// and the saturating e4m3x2 conversion replaces the clamp to +-448 (values
 // beyond 448 round to 448 either way).
 constexpr int kHeadBlock = 4;
 
+template <int V>
 __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a, int group) {
   const int slot = blockIdx.y;
   const int lane = threadIdx.x & 31;
@@ -209,58 +210,82 @@ __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a
   const uint32_t bat = pr - q2 * a.div_batch.d;
   const uint32_t peer = fast_div(q2, a.div_seq);
   const uint32_t s = q2 - peer * a.div_seq.d;
-  const int c0 = sub * 8;
+  const int c0 = sub * 8 * V;
   const bool has = live && c0 < a.width && static_cast<int64_t>(peer) * a.seq + s < a.valid_seq;
   const bool rope = has && slot < 2 && c0 < a.rotary;
-  const int64_t half = a.rotary / 2;
+  const int half = static_cast<int>(a.rotary / 2);
   const bool first = c0 < half;
-  uint32_t cw[4] = {0, 0, 0, 0}, sw[4] = {0, 0, 0, 0};
-  if (rope)
-    load_cos_sin8(a.cos + static_cast<int64_t>(s) * a.rotary + c0, a.sin + static_cast<int64_t>(s) * a.rotary + c0,
-                  cw, sw);
+  uint32_t cw[V][4], sw[V][4];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    if (rope) {
+      load_cos_sin8(a.cos + static_cast<int64_t>(s) * a.rotary + c0 + 8 * v,
+                    a.sin + static_cast<int64_t>(s) * a.rotary + c0 + 8 * v, cw[v], sw[v]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cw[v][k] = sw[v][k] = 0;
+    }
+  }
   const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(a.src[slot]) + peer * a.st[slot][0] +
-                              s * a.st[slot][1] + bat * a.st[slot][2];
-  const int64_t pofs = first ? half : -half;
+                              s * a.st[slot][1] + bat * a.st[slot][2] + c0;
+  const int pofs = first ? half : -half;
+  const int64_t hstride = a.st[slot][3];
   constexpr float kRcp448 = 1.0f / 448.0f;  // RN(1/448)
-  const int64_t wire_base = (static_cast<int64_t>(peer) * (a.streams - 1) + slot) * a.peer_rows;
-  for (int64_t h0 = 0; h0 < a.heads; h0 += kHeadBlock) {
-    uint4 raw[kHeadBlock], par[kHeadBlock];
+  const int64_t row_bytes = a.width + 4;
+  uint8_t* dst0 = a.payload + ((static_cast<int64_t>(peer) * (a.streams - 1) + slot) * a.peer_rows + pos * a.heads) * row_bytes +
+                  static_cast<int64_t>(peer) * a.peer_padding;
+  const int heads = static_cast<int>(a.heads);
+  for (int h0 = 0; h0 < heads; h0 += kHeadBlock) {
+    uint4 raw[kHeadBlock][V], par[kHeadBlock][V];
 #pragma unroll
     for (int j = 0; j < kHeadBlock; ++j) {
-      const bool hj = has && h0 + j < a.heads;
-      const __nv_bfloat16* src = base + (h0 + j) * a.st[slot][3] + c0;
-      raw[j] = hj ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0, 0, 0, 0);
-      par[j] = hj && rope ? __ldg(reinterpret_cast<const uint4*>(src + pofs)) : make_uint4(0, 0, 0, 0);
+      const bool hj = has && h0 + j < heads;
+      const __nv_bfloat16* src = base + (h0 + j) * hstride;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        raw[j][v] = hj ? __ldg(reinterpret_cast<const uint4*>(src) + v) : make_uint4(0, 0, 0, 0);
+        par[j][v] = hj && rope ? __ldg(reinterpret_cast<const uint4*>(src + pofs) + v) : make_uint4(0, 0, 0, 0);
+      }
     }
 #pragma unroll
     for (int j = 0; j < kHeadBlock; ++j) {
-      if (h0 + j >= a.heads) break;  // uniform across the warp
-      if (rope) raw[j] = rope8_bf16(raw[j], par[j], first, cw, sw);
-      float x[8];
-      unpack_bf16x8(raw[j], x);
-      float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fabsf(x[2]));
-      m = fmaxf(fmaxf(m, fabsf(x[3])), fabsf(x[4]));
-      m = fmaxf(fmaxf(m, fabsf(x[5])), fmaxf(fabsf(x[6]), fabsf(x[7])));
+      if (h0 + j >= heads) break;  // uniform across the warp
+      float x[V][8];
+      float m = 0.f;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        if (rope) raw[j][v] = rope8_bf16(raw[j][v], par[j][v], first, cw[v], sw[v]);
+        unpack_bf16x8(raw[j][v], x[v]);
+        m = fmaxf(fmaxf(m, fabsf(x[v][0])), fabsf(x[v][1]));
+        m = fmaxf(fmaxf(m, fabsf(x[v][2])), fabsf(x[v][3]));
+        m = fmaxf(fmaxf(m, fabsf(x[v][4])), fabsf(x[v][5]));
+        m = fmaxf(fmaxf(m, fabsf(x[v][6])), fabsf(x[v][7]));
+      }
       for (int o = group / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       const float scale = fmaxf(div_by(m, 448.0f, kRcp448), 1.0e-12f);
       if (!live) continue;
-      const int64_t row = pos * a.heads + h0 + j;
-      uint8_t* dst = a.payload + (row + wire_base) * (a.width + 4) + static_cast<int64_t>(peer) * a.peer_padding;
+      uint8_t* dst = dst0 + (h0 + j) * row_bytes;
       if (c0 < a.width) {
         const float y = __frcp_rn(scale);
-        const uint32_t e0 = e4m3x2(div_by(x[0], scale, y), div_by(x[1], scale, y));
-        const uint32_t e1 = e4m3x2(div_by(x[2], scale, y), div_by(x[3], scale, y));
-        const uint32_t e2 = e4m3x2(div_by(x[4], scale, y), div_by(x[5], scale, y));
-        const uint32_t e3 = e4m3x2(div_by(x[6], scale, y), div_by(x[7], scale, y));
-        // Rows start at 4-byte multiples (width % 4 == 0), so two u32 stores.
-        reinterpret_cast<uint32_t*>(dst + c0)[0] = e0 | (e1 << 16);
-        reinterpret_cast<uint32_t*>(dst + c0)[1] = e2 | (e3 << 16);
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          const uint32_t e0 = e4m3x2(div_by(x[v][0], scale, y), div_by(x[v][1], scale, y));
+          const uint32_t e1 = e4m3x2(div_by(x[v][2], scale, y), div_by(x[v][3], scale, y));
+          const uint32_t e2 = e4m3x2(div_by(x[v][4], scale, y), div_by(x[v][5], scale, y));
+          const uint32_t e3 = e4m3x2(div_by(x[v][6], scale, y), div_by(x[v][7], scale, y));
+          // Rows start at 4-byte multiples (width % 4 == 0), so u32 stores.
+          reinterpret_cast<uint32_t*>(dst + c0 + 8 * v)[0] = e0 | (e1 << 16);
+          reinterpret_cast<uint32_t*>(dst + c0 + 8 * v)[1] = e2 | (e3 << 16);
+        }
       }
       if (sub == 0) *reinterpret_cast<float*>(dst + a.width) = scale;
-      if (a.peer_padding && sub == 0 && slot == 0 && row % a.peer_rows == 0) {
-        const int64_t packet = a.peer_rows * a.streams * (a.width + 4);
-        uint8_t* tail = a.payload + static_cast<int64_t>(peer) * (packet + a.peer_padding) + packet;
-        for (int64_t i = 0; i < a.peer_padding; ++i) tail[i] = 0;
+      if (a.peer_padding && sub == 0 && slot == 0) {
+        const int64_t row = pos * a.heads + h0 + j;
+        if (row % a.peer_rows == 0) {
+          const int64_t packet = a.peer_rows * a.streams * row_bytes;
+          uint8_t* tail = a.payload + static_cast<int64_t>(peer) * (packet + a.peer_padding) + packet;
+          for (int64_t i = 0; i < a.peer_padding; ++i) tail[i] = 0;
+        }
       }
     }
   }
@@ -379,9 +404,14 @@ XGB_API int xgb_fp8_wire_encode_view(const void* const* sources, const int64_t* 
   dim3 grid(static_cast<unsigned>(cdiv(a.rows, rows_per_block)), streams);
   cudaStream_t st = as_stream(stream);
   if (dtype == XGB_BF16) {
-    if (vec && rotary % 16 == 0) {
+    if (vec && width % 16 == 0 && rotary % 32 == 0 && heads <= INT32_MAX) {
+      int g2 = 1;  // lanes per row at 16 channels per lane
+      while (g2 < width / 16) g2 <<= 1;
+      const dim3 pgrid(static_cast<unsigned>(cdiv(a.rows / heads, (kThreads / 32) * (32 / g2))), streams);
+      wire_encode_bf16_kernel<2><<<pgrid, kThreads, 0, st>>>(a, g2);
+    } else if (vec && rotary % 16 == 0 && heads <= INT32_MAX) {
       const dim3 pgrid(static_cast<unsigned>(cdiv(a.rows / heads, rows_per_block)), streams);
-      wire_encode_bf16_kernel<<<pgrid, kThreads, 0, st>>>(a, group);
+      wire_encode_bf16_kernel<1><<<pgrid, kThreads, 0, st>>>(a, group);
     }
     else if (vec) wire_encode_kernel<__nv_bfloat16, true><<<grid, kThreads, 0, st>>>(a, group);
     else wire_encode_kernel<__nv_bfloat16, false><<<grid, kThreads, 0, st>>>(a, group);
