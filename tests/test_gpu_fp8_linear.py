@@ -134,3 +134,40 @@ def test_swiglu_epilogue_matches_gemm_then_swiglu(cuda_device, scaling):
                        gate_first_swiglu(plain.forward_quantized(q, s)))
     with pytest.raises(ValueError):
         plain.forward_quantized(q, s, activation=3)
+
+
+@pytest.mark.parametrize("m,n,k", [(129, 256, 208), (257, 272, 3072), (1000, 3072, 256),
+                                   (15845, 512, 3072)])
+def test_cta_pair_gemm_matches_single_cta(cuda_device, monkeypatch, m, n, k):
+    """The CTA-pair kernel (cta_group::2, M > 128) gives the same bits as the
+    1-CTA kernel for every epilogue, including M, N and K tails: both
+    accumulate each output over K in the same order."""
+    from xgen_b200.fp8_linear import H3FP8Linear
+    from xgen_b200.ops import quantize_per_token
+
+    g = torch.Generator().manual_seed(m + n + k)
+    w = (torch.randn(n, k, generator=g) * 0.03).bfloat16()
+    bias = torch.randn(n, generator=g).bfloat16()
+    layer = H3FP8Linear(w, bias, scaling="per_token").to(cuda_device)
+    x = torch.randn(m, k, generator=g).bfloat16().to(cuda_device)
+    q, s = quantize_per_token(x)
+    res = torch.randn(1, m, n, generator=g).bfloat16().to(cuda_device)
+    gate = torch.randn(3, n, generator=g).bfloat16().to(cuda_device)
+    idx = torch.randint(3, (m,), generator=g).to(cuda_device)
+
+    def run():
+        out = [layer.forward_quantized(q, s), layer.forward_quantized(q, s, activation=1),
+               layer.forward_gated(x.unsqueeze(0), gate, idx, res)]
+        if n % 256 == 0:
+            out.append(layer.swiglu_interleaved().forward_quantized(q, s, activation=3))
+        torch.cuda.synchronize()
+        return out
+
+    monkeypatch.setenv("XGB_GEMM_CTA_PAIRS", "0")
+    single = run()
+    monkeypatch.setenv("XGB_GEMM_CTA_PAIRS", "1")
+    pair = run()
+    from xgen_b200.attention import kernel_errors
+    assert kernel_errors() == 0
+    for a, b in zip(single, pair):
+        assert torch.equal(a, b)

@@ -27,6 +27,8 @@
 //              AdaLN gate and residual move as 16-byte vectors
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile run
 // under the MMAs of the next. Every mbarrier wait is bounded.
+#include <cstdlib>
+
 #include "sm100.cuh"
 #include "tma_host.h"
 
@@ -89,6 +91,128 @@ struct Barriers {
   uint64_t end;
   uint32_t tmem_base;
 };
+
+// One accumulator tile's epilogue for the output row `m` this thread owns
+// (its TMEM lane) and the column half `half`: reads the fp32 accumulators at
+// TMEM address `acc` and writes the bf16 outputs with the kEpi epilogue.
+template <int kEpi>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t acc, int m, int n0, int half) {
+  const bool row_ok = m < p.M;
+  const float sa = row_ok ? p.sa[m * p.sa_stride] : 0.f;
+  const int64_t grow = (kEpi == kGated && row_ok) ? p.idx[m] : 0;
+  if constexpr (kEpi == kSwiGLU) {
+    // N % 256 == 0 (checked on the host): gate columns n0 + [0, 128),
+    // value columns n0 + [128, 256), outputs n0/2 + [0, 128).
+#pragma unroll 1
+    for (int c = half * (kBN / 128); c < (half + 1) * (kBN / 128); ++c) {
+      uint32_t rg[32], rv[32];
+      tmem_ld32(acc + c * 32, rg);
+      tmem_ld32(acc + kBN / 2 + c * 32, rv);
+      tmem_ld_wait();
+      if (row_ok) {
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float y[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int ng = n0 + c * 32 + e + u, nv = ng + kBN / 2;
+            const float bg = p.bias ? __bfloat162float(p.bias[ng]) : 0.f;
+            const float bv = p.bias ? __bfloat162float(p.bias[nv]) : 0.f;
+            const float g = bf16_round(fmaf(__uint_as_float(rg[e + u]), sa * p.sb[ng * p.sb_stride], bg));
+            const float v = bf16_round(fmaf(__uint_as_float(rv[e + u]), sa * p.sb[nv * p.sb_stride], bv));
+            y[u] = swiglu_pair(g, v);
+          }
+          w[e / 2] = pack_bf16x2(y[0], y[1]);
+        }
+        uint4* d4 = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m) * p.ldo + n0 / 2 + c * 32);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+      }
+    }
+  } else {
+#pragma unroll 1
+  for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
+    uint32_t r[32];
+    tmem_ld32(acc + c * 32, r);
+    tmem_ld_wait();
+    const int nb = n0 + c * 32;
+    if (row_ok && p.vec && nb + 32 <= p.N) {
+      // 8 columns at a time: scales, bias, gate row and residual as vectors
+      __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
+#pragma unroll
+      for (int g8 = 0; g8 < 4; ++g8) {
+        const int n = nb + g8 * 8;
+        float alpha[8], bias[8], y[8];
+        if (p.sb_stride) {
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.sb + n));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.sb + n + 4));
+          alpha[0] = sa * b0.x; alpha[1] = sa * b0.y; alpha[2] = sa * b0.z; alpha[3] = sa * b0.w;
+          alpha[4] = sa * b1.x; alpha[5] = sa * b1.y; alpha[6] = sa * b1.z; alpha[7] = sa * b1.w;
+        } else {
+          const float al = sa * p.sb[0];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) alpha[i] = al;
+        }
+        if (p.bias) {
+          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.bias + n)), bias);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) bias[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          y[i] = fmaf(__uint_as_float(r[g8 * 8 + i]), alpha[i], bias[i]);
+          if constexpr (kEpi == kGeluErf) y[i] = gelu_erf(y[i]);
+          if constexpr (kEpi == kGeluTanh) y[i] = gelu_tanh(y[i]);
+        }
+        if constexpr (kEpi == kGated) {
+          // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
+          float gt[8], res[8];
+          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.ldg + n)), gt);
+          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(m) * p.ldr + n)), res);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[i]), gt[i])), res[i]);
+        }
+        reinterpret_cast<uint4*>(dst)[g8] =
+            make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                       pack_bf16x2(y[6], y[7]));
+      }
+    } else if (row_ok && nb < p.N) {
+      uint32_t w[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float y[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int n = min(nb + e + u, p.N - 1);
+          const float alpha = sa * p.sb[n * p.sb_stride];
+          const float bias = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+          y[u] = fmaf(__uint_as_float(r[e + u]), alpha, bias);
+          if constexpr (kEpi == kGeluErf) y[u] = gelu_erf(y[u]);
+          if constexpr (kEpi == kGeluTanh) y[u] = gelu_tanh(y[u]);
+          if constexpr (kEpi == kGated) {
+            // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
+            const float g = __bfloat162float(p.gate[grow * p.ldg + n]);
+            const float res = __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + n]);
+            y[u] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[u]), g)), res);
+          }
+        }
+        w[e / 2] = pack_bf16x2(y[0], y[1]);
+      }
+      __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
+      if (nb + 32 <= p.N) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+      } else {
+        const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+        for (int e = 0; e < p.N - nb; ++e) dst[e] = wb[e];
+      }
+    }
+  }
+  }
+}
 
 template <int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -192,123 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = (t / n_tiles) * kBM + quarter * 32 + lane;
       const int n0 = (t % n_tiles) * kBN;
-      const bool row_ok = m < p.M;
-      const float sa = row_ok ? p.sa[m * p.sa_stride] : 0.f;
-      const int64_t grow = (kEpi == kGated && row_ok) ? p.idx[m] : 0;
-      if constexpr (kEpi == kSwiGLU) {
-        // N % 256 == 0 (checked on the host): gate columns n0 + [0, 128),
-        // value columns n0 + [128, 256), outputs n0/2 + [0, 128).
-#pragma unroll 1
-        for (int c = half * (kBN / 128); c < (half + 1) * (kBN / 128); ++c) {
-          uint32_t rg[32], rv[32];
-          tmem_ld32(lane_addr + a * kBN + c * 32, rg);
-          tmem_ld32(lane_addr + a * kBN + kBN / 2 + c * 32, rv);
-          tmem_ld_wait();
-          if (row_ok) {
-            uint32_t w[16];
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              float y[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int ng = n0 + c * 32 + e + u, nv = ng + kBN / 2;
-                const float bg = p.bias ? __bfloat162float(p.bias[ng]) : 0.f;
-                const float bv = p.bias ? __bfloat162float(p.bias[nv]) : 0.f;
-                const float g = bf16_round(fmaf(__uint_as_float(rg[e + u]), sa * p.sb[ng * p.sb_stride], bg));
-                const float v = bf16_round(fmaf(__uint_as_float(rv[e + u]), sa * p.sb[nv * p.sb_stride], bv));
-                y[u] = swiglu_pair(g, v);
-              }
-              w[e / 2] = pack_bf16x2(y[0], y[1]);
-            }
-            uint4* d4 = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m) * p.ldo + n0 / 2 + c * 32);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(&bars->acc_empty[a]);
-        continue;
-      }
-#pragma unroll 1
-      for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_addr + a * kBN + c * 32, r);
-        tmem_ld_wait();
-        const int nb = n0 + c * 32;
-        if (row_ok && p.vec && nb + 32 <= p.N) {
-          // 8 columns at a time: scales, bias, gate row and residual as vectors
-          __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
-#pragma unroll
-          for (int g8 = 0; g8 < 4; ++g8) {
-            const int n = nb + g8 * 8;
-            float alpha[8], bias[8], y[8];
-            if (p.sb_stride) {
-              const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.sb + n));
-              const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.sb + n + 4));
-              alpha[0] = sa * b0.x; alpha[1] = sa * b0.y; alpha[2] = sa * b0.z; alpha[3] = sa * b0.w;
-              alpha[4] = sa * b1.x; alpha[5] = sa * b1.y; alpha[6] = sa * b1.z; alpha[7] = sa * b1.w;
-            } else {
-              const float al = sa * p.sb[0];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) alpha[i] = al;
-            }
-            if (p.bias) {
-              unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.bias + n)), bias);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 8; ++i) bias[i] = 0.f;
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              y[i] = fmaf(__uint_as_float(r[g8 * 8 + i]), alpha[i], bias[i]);
-              if constexpr (kEpi == kGeluErf) y[i] = gelu_erf(y[i]);
-              if constexpr (kEpi == kGeluTanh) y[i] = gelu_tanh(y[i]);
-            }
-            if constexpr (kEpi == kGated) {
-              // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
-              float gt[8], res[8];
-              unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.ldg + n)), gt);
-              unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(m) * p.ldr + n)), res);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[i]), gt[i])), res[i]);
-            }
-            reinterpret_cast<uint4*>(dst)[g8] =
-                make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
-                           pack_bf16x2(y[6], y[7]));
-          }
-        } else if (row_ok && nb < p.N) {
-          uint32_t w[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float y[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int n = min(nb + e + u, p.N - 1);
-              const float alpha = sa * p.sb[n * p.sb_stride];
-              const float bias = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
-              y[u] = fmaf(__uint_as_float(r[e + u]), alpha, bias);
-              if constexpr (kEpi == kGeluErf) y[u] = gelu_erf(y[u]);
-              if constexpr (kEpi == kGeluTanh) y[u] = gelu_tanh(y[u]);
-              if constexpr (kEpi == kGated) {
-                // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
-                const float g = __bfloat162float(p.gate[grow * p.ldg + n]);
-                const float res = __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + n]);
-                y[u] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[u]), g)), res);
-              }
-            }
-            w[e / 2] = pack_bf16x2(y[0], y[1]);
-          }
-          __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
-          if (nb + 32 <= p.N) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
-          } else {
-            const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
-            for (int e = 0; e < p.N - nb; ++e) dst[e] = wb[e];
-          }
-        }
-      }
+      epilogue_tile<kEpi>(p, lane_addr + a * kBN, m, n0, half);
       tc_fence_before();
       mbar_arrive(&bars->acc_empty[a]);
     }
@@ -321,11 +329,197 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- CTA pairs
+// The same GEMM on CTA pairs (cta_group::2): a pair computes a 256 x 256
+// tile with M256 N256 K32 MMAs issued by rank 0. Each CTA loads its own 128
+// rows of A and its own 128 of the tile's 256 W rows per stage (32 KB), so
+// a pair moves 64 KB per k-block for twice the work of one 1-CTA stage
+// (48 KB): per SM a third less L2-to-SM traffic, and 6 stages in flight.
+// Each CTA's TMEM holds its 128 output rows x 256 columns, so the epilogue
+// is the 1-CTA one on rows m0 + 128 * rank.
+//
+// Pair protocol (every wait bounded):
+//   full[s]      rank 0 only: rank 0's producer expects 64 KB, both CTAs'
+//                TMA loads count their bytes on it
+//   empty[s]     per CTA: the MMA commits to both CTAs' barriers
+//   acc_full[a]  per CTA: the MMA commits to both
+//   acc_empty[a] rank 0: 16 arrivals, one per epilogue warp of both CTAs
+//   end          per CTA: the MMA's last commit; TMEM is freed after it
+// A cluster barrier after the barrier inits and one before exit keep both
+// CTAs alive while the other may still signal them.
+constexpr int kPairStages = 6;
+constexpr int kPairRows = 128;                      // A rows and W rows per CTA
+constexpr int kPairABytes = kPairRows * kBK;        // 16 KB
+constexpr int kPairStageBytes = 2 * kPairRows * kBK;  // 32 KB
+constexpr int kPairBarOff = kPairStages * kPairStageBytes;
+constexpr int kPairSmem = kPairBarOff + 256 + 1024;
+constexpr uint32_t kPairIdesc = instr_desc(1, 0, 0, false, false, 2 * kPairRows, kBN);
+
+struct PairBarriers {
+  uint64_t full[kPairStages];
+  uint64_t empty[kPairStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t end;
+  uint32_t tmem_base;
+};
+
+template <int kEpi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap a_map,
+                         const __grid_constant__ CUtensorMap b_map, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  PairBarriers* bars = reinterpret_cast<PairBarriers*>(smem + kPairBarOff);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+  const int m_tiles = (p.M + 2 * kPairRows - 1) / (2 * kPairRows);
+  const int n_tiles = (p.N + kBN - 1) / kBN;
+  const int tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 2 * (kEpiThreads / 32));
+    }
+    mbar_init(&bars->end, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair<512>(&bars->tmem_base);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&a_map);
+    prefetch_tmap(&b_map);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    if (lane == 0) {
+      bool ok = true;
+      int it = 0;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        const int m0 = (t / n_tiles) * 2 * kPairRows + static_cast<int>(rank) * kPairRows;
+        const int n0 = (t % n_tiles) * kBN + static_cast<int>(rank) * kPairRows;
+        for (int kb = 0; kb < k_blocks && ok; ++kb, ++it) {
+          const int s = it % kPairStages;
+          if (it >= kPairStages) ok = mbar_wait(&bars->empty[s], ((it / kPairStages) - 1) & 1, p.err);
+          if (!ok) break;
+          uint8_t* st = smem + s * kPairStageBytes;
+          const uint32_t full0 = map_to_rank(&bars->full[s], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairStageBytes);
+          tma_load_2d_pair(st, &a_map, full0, kb * kBK, m0);
+          tma_load_2d_pair(st + kPairABytes, &b_map, full0, kb * kBK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (rank 0)
+    if (lane == 0 && rank == 0) {
+      bool ok = true;
+      int it = 0, lt = 0;
+      for (int t = pair; t < tiles && ok; t += pairs, ++lt) {
+        const int a = lt & 1;
+        if (lt >= 2) ok = mbar_wait(&bars->acc_empty[a], ((lt >> 1) - 1) & 1, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + a * kBN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % kPairStages;
+          ok = mbar_wait(&bars->full[s], (it / kPairStages) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t as = smem_u32(smem + s * kPairStageBytes);
+          const uint32_t bs = as + kPairABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            mma_pair_f8f6f4(d, smem_desc_sw128(as + k * 32, 16, 1024),
+                            smem_desc_sw128(bs + k * 32, 16, 1024), kPairIdesc, kb > 0 || k > 0);
+          tc_commit_pair(map_to_rank(&bars->empty[s], 0));
+          tc_commit_pair(map_to_rank(&bars->empty[s], 1));
+        }
+        if (!ok) break;
+        tc_commit_pair(map_to_rank(&bars->acc_full[a], 0));
+        tc_commit_pair(map_to_rank(&bars->acc_full[a], 1));
+      }
+      tc_commit_pair(map_to_rank(&bars->end, 0));
+      tc_commit_pair(map_to_rank(&bars->end, 1));
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    int lt = 0;
+    for (int t = pair; t < tiles; t += pairs, ++lt) {
+      const int a = lt & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[a], (lt >> 1) & 1, p.err));
+      if (!ok) break;
+      tc_fence_after();
+      const int m = (t / n_tiles) * 2 * kPairRows + static_cast<int>(rank) * kPairRows + quarter * 32 + lane;
+      const int n0 = (t % n_tiles) * kBN;
+      epilogue_tile<kEpi>(p, lane_addr + a * kBN, m, n0, half);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(&bars->acc_empty[a], 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // every pair MMA (which reads both CTAs' shared memory) has ended
+    mbar_wait(&bars->end, 0, p.err, 100000000ull);
+    tc_fence_after();
+    tmem_dealloc_pair<512>(tmem);
+  }
+  cluster_sync();
+}
+
 int sm_count() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 148;
+}
+
+// CTA pairs are used for M > 128 unless XGB_GEMM_CTA_PAIRS=0 (read per call).
+bool pairs_enabled() {
+  const char* v = std::getenv("XGB_GEMM_CTA_PAIRS");
+  return !(v && v[0] == '0');
+}
+
+// Pairs of this kernel that can be resident at once (0 if the pair launch is
+// unavailable): the persistent grid is sized to it so no pair waits for
+// another to finish.
+template <typename Kernel>
+int pair_slots(Kernel kernel) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem) != cudaSuccess)
+    return 0;
+  static int cached = -1;  // one per kernel instantiation; every B200 has the same SMs
+  if (cached >= 0) return cached;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * static_cast<unsigned>(sm_count()));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmem;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    clusters = 0;
+  }
+  cached = clusters;
+  return clusters;
 }
 
 template <int kEpi>
@@ -339,6 +533,21 @@ int launch(const void* a, const void* w, const Params& p, cudaStream_t st) {
   if (!make_tensor_map(&am, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, adims, astr, abox) ||
       !make_tensor_map(&bm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, bdims, astr, bbox))
     return XGB_ERR_ALIGN;
+  if (p.M > kBM && pairs_enabled()) {
+    // CTA pairs: W tiles of 128 rows per CTA
+    CUtensorMap bm2;
+    const uint32_t bbox2[2] = {kBK, kPairRows};
+    if (!make_tensor_map(&bm2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, bdims, astr, bbox2))
+      return XGB_ERR_ALIGN;
+    auto kernel = gemm_fp8_pair_kernel<kEpi>;
+    const int max_pairs = pair_slots(kernel);
+    if (max_pairs > 0) {
+      const int tiles = ((p.M + 2 * kPairRows - 1) / (2 * kPairRows)) * ((p.N + kBN - 1) / kBN);
+      const int grid = 2 * std::min(tiles, max_pairs);
+      kernel<<<grid, kThreads, kPairSmem, st>>>(am, bm2, p);
+      return launch_status();
+    }
+  }
   auto kernel = gemm_fp8_kernel<kEpi>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
     return XGB_ERR_LAUNCH;
