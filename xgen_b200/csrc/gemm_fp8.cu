@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // tile with M256 N256 K32 MMAs issued by rank 0. Each CTA loads its own 128
 // rows of A and its own 128 of the tile's 256 W rows per stage (32 KB), so
 // a pair moves 64 KB per k-block for twice the work of one 1-CTA stage
-// (48 KB): per SM a third less L2-to-SM traffic, and 6 stages in flight.
+// (48 KB): per SM a third less L2-to-SM traffic, and 7 stages (224 KB) in flight.
 // Each CTA's TMEM holds its 128 output rows x 256 columns, so the epilogue
 // is the 1-CTA one on rows m0 + 128 * rank.
 //
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   end          per CTA: the MMA's last commit; TMEM is freed after it
 // A cluster barrier after the barrier inits and one before exit keep both
 // CTAs alive while the other may still signal them.
-constexpr int kPairStages = 6;
+constexpr int kPairStages = 7;
 constexpr int kPairRows = 128;                      // A rows and W rows per CTA
 constexpr int kPairABytes = kPairRows * kBK;        // 16 KB
 constexpr int kPairStageBytes = 2 * kPairRows * kBK;  // 32 KB

@@ -155,10 +155,10 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 
 // ---------------------------------------------------------------- CTA pairs (cta_group::2)
 // A cluster of two CTAs on neighbouring SMs sharing one tcgen05 MMA: rank 0
-// issues the MMAs over both CTAs' shared memory and TMEM. No load here uses
-// cluster multicast: each CTA's TMA writes only its own shared memory and
-// signals the rank-0 barrier, and the MMA signals each CTA's barrier with
-// its own commit.
+// issues the MMAs over both CTAs' shared memory and TMEM. No load here is
+// broadcast to several CTAs: each CTA's TMA writes only its own shared
+// memory and signals the rank-0 barrier, and the MMA signals each CTA's
+// barrier with its own commit.
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
