@@ -87,9 +87,14 @@ def _worker(rank, world, port, q, k, v, cos, sin, results):
 
 
 @pytest.mark.parametrize("s", [1022, 1024])
-def test_sp2_fp8_phaa_matches_single_gpu(cuda_device, s):
+def test_sp2_fp8_phaa_matches_single_gpu(cuda_device, monkeypatch, s):
+    """SP2 over NCCL equals one GPU bit for bit. The attention tail split is
+    off on both sides (XGB_ATTN_TAIL_SPLIT=0, inherited by the spawned
+    ranks): with it, a launch's split plan depends on how many heads it
+    holds, and Sage split parts quantise P against their own running max."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    monkeypatch.setenv("XGB_ATTN_TAIL_SPLIT", "0")
     q, k, v, cos, sin = _inputs(s)
     expect = _single_gpu_reference(q, k, v, cos, sin)
     ctx = mp.get_context("spawn")

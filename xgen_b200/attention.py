@@ -13,6 +13,7 @@ does at x_base/x_base/operator/attention.py:357-362).
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
@@ -57,6 +58,12 @@ def kernel_errors(device: torch.device | None = None) -> int:
 
 
 def _ws_args(device: torch.device):
+    """Tail-split workspace arguments. XGB_ATTN_TAIL_SPLIT=0 passes none,
+    which turns the split off: the Sage result then no longer depends on how
+    many (batch, head) items a launch holds (split parts quantise P against
+    their own running max), e.g. for bit-identical results across SP degrees."""
+    if os.environ.get("XGB_ATTN_TAIL_SPLIT", "1") == "0":
+        return None, 0
     ws = _split_ws(device)
     return ws.data_ptr(), ws.numel()
 
