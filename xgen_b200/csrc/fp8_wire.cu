@@ -188,13 +188,14 @@ __global__ void __launch_bounds__(kThreads) wire_encode_kernel(EncodeArgs a, int
 // its heads kHeadBlock at a time, each lane 8V channels (V 16-byte words),
 // so the position's cos/sin are read once for all heads, the per-row index
 // and scale work is shared by 8V channels, and each lane has several row
-// loads in flight. The row stays packed bf16x2: the RoPE products and sum
+// loads in flight; the RoPE partner channels come from the partner lane by
+// shuffle. The row stays packed bf16x2: the RoPE products and sum
 // are bf16x2 operations (rope8_bf16), the row scale's division by 448 and
 // the per-element x / scale are Markstein-corrected reciprocal multiplies
 // (the correctly rounded quotient; below 448e-12 the 1e-12 floor decides),
 // and the saturating e4m3x2 conversion replaces the clamp to +-448 (values
 // beyond 448 round to 448 either way).
-constexpr int kHeadBlock = 4;
+constexpr int kHeadBlock = 3;  // H3 has 24 heads: 3, 6, 12 or 24 per rank
 
 template <int V>
 __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a, int group) {
@@ -228,7 +229,9 @@ __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a
   }
   const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(a.src[slot]) + peer * a.st[slot][0] +
                               s * a.st[slot][1] + bat * a.st[slot][2] + c0;
-  const int pofs = first ? half : -half;
+  // The partner channels c -/+ rotary/2 sit in the lane rotary/(16V) away
+  // within the row group (rotary % (16V) == 0); they come by shuffle.
+  const int plane = (lane & ~(group - 1)) | (c0 >= a.rotary ? sub : (first ? sub + half / (8 * V) : sub - half / (8 * V)));
   const int64_t hstride = a.st[slot][3];
   constexpr float kRcp448 = 1.0f / 448.0f;  // RN(1/448)
   const int64_t row_bytes = a.width + 4;
@@ -236,16 +239,14 @@ __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a
                   static_cast<int64_t>(peer) * a.peer_padding;
   const int heads = static_cast<int>(a.heads);
   for (int h0 = 0; h0 < heads; h0 += kHeadBlock) {
-    uint4 raw[kHeadBlock][V], par[kHeadBlock][V];
+    uint4 raw[kHeadBlock][V];
 #pragma unroll
     for (int j = 0; j < kHeadBlock; ++j) {
       const bool hj = has && h0 + j < heads;
       const __nv_bfloat16* src = base + (h0 + j) * hstride;
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
+      for (int v = 0; v < V; ++v)
         raw[j][v] = hj ? __ldg(reinterpret_cast<const uint4*>(src) + v) : make_uint4(0, 0, 0, 0);
-        par[j][v] = hj && rope ? __ldg(reinterpret_cast<const uint4*>(src + pofs) + v) : make_uint4(0, 0, 0, 0);
-      }
     }
 #pragma unroll
     for (int j = 0; j < kHeadBlock; ++j) {
@@ -254,7 +255,14 @@ __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a
       float m = 0.f;
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        if (rope) raw[j][v] = rope8_bf16(raw[j][v], par[j][v], first, cw[v], sw[v]);
+        if (slot < 2 && a.rotary > 0) {  // uniform: every lane of the group shuffles
+          uint4 par;
+          par.x = __shfl_sync(0xffffffffu, raw[j][v].x, plane);
+          par.y = __shfl_sync(0xffffffffu, raw[j][v].y, plane);
+          par.z = __shfl_sync(0xffffffffu, raw[j][v].z, plane);
+          par.w = __shfl_sync(0xffffffffu, raw[j][v].w, plane);
+          if (rope) raw[j][v] = rope8_bf16(raw[j][v], par, first, cw[v], sw[v]);
+        }
         unpack_bf16x8(raw[j][v], x[v]);
         m = fmaxf(fmaxf(m, fabsf(x[v][0])), fabsf(x[v][1]));
         m = fmaxf(fmaxf(m, fabsf(x[v][2])), fabsf(x[v][3]));

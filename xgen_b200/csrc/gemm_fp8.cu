@@ -132,85 +132,85 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t acc, int
     }
   } else {
 #pragma unroll 1
-  for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
-    uint32_t r[32];
-    tmem_ld32(acc + c * 32, r);
-    tmem_ld_wait();
-    const int nb = n0 + c * 32;
-    if (row_ok && p.vec && nb + 32 <= p.N) {
-      // 8 columns at a time: scales, bias, gate row and residual as vectors
-      __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
+    for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(acc + c * 32, r);
+      tmem_ld_wait();
+      const int nb = n0 + c * 32;
+      if (row_ok && p.vec && nb + 32 <= p.N) {
+        // 8 columns at a time: scales, bias, gate row and residual as vectors
+        __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
 #pragma unroll
-      for (int g8 = 0; g8 < 4; ++g8) {
-        const int n = nb + g8 * 8;
-        float alpha[8], bias[8], y[8];
-        if (p.sb_stride) {
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.sb + n));
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.sb + n + 4));
-          alpha[0] = sa * b0.x; alpha[1] = sa * b0.y; alpha[2] = sa * b0.z; alpha[3] = sa * b0.w;
-          alpha[4] = sa * b1.x; alpha[5] = sa * b1.y; alpha[6] = sa * b1.z; alpha[7] = sa * b1.w;
-        } else {
-          const float al = sa * p.sb[0];
+        for (int g8 = 0; g8 < 4; ++g8) {
+          const int n = nb + g8 * 8;
+          float alpha[8], bias[8], y[8];
+          if (p.sb_stride) {
+            const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.sb + n));
+            const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.sb + n + 4));
+            alpha[0] = sa * b0.x; alpha[1] = sa * b0.y; alpha[2] = sa * b0.z; alpha[3] = sa * b0.w;
+            alpha[4] = sa * b1.x; alpha[5] = sa * b1.y; alpha[6] = sa * b1.z; alpha[7] = sa * b1.w;
+          } else {
+            const float al = sa * p.sb[0];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) alpha[i] = al;
-        }
-        if (p.bias) {
-          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.bias + n)), bias);
-        } else {
+            for (int i = 0; i < 8; ++i) alpha[i] = al;
+          }
+          if (p.bias) {
+            unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.bias + n)), bias);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) bias[i] = 0.f;
-        }
+            for (int i = 0; i < 8; ++i) bias[i] = 0.f;
+          }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          y[i] = fmaf(__uint_as_float(r[g8 * 8 + i]), alpha[i], bias[i]);
-          if constexpr (kEpi == kGeluErf) y[i] = gelu_erf(y[i]);
-          if constexpr (kEpi == kGeluTanh) y[i] = gelu_tanh(y[i]);
-        }
-        if constexpr (kEpi == kGated) {
-          // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
-          float gt[8], res[8];
-          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.ldg + n)), gt);
-          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(m) * p.ldr + n)), res);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[i]), gt[i])), res[i]);
-        }
-        reinterpret_cast<uint4*>(dst)[g8] =
-            make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
-                       pack_bf16x2(y[6], y[7]));
-      }
-    } else if (row_ok && nb < p.N) {
-      uint32_t w[16];
-#pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        float y[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int n = min(nb + e + u, p.N - 1);
-          const float alpha = sa * p.sb[n * p.sb_stride];
-          const float bias = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
-          y[u] = fmaf(__uint_as_float(r[e + u]), alpha, bias);
-          if constexpr (kEpi == kGeluErf) y[u] = gelu_erf(y[u]);
-          if constexpr (kEpi == kGeluTanh) y[u] = gelu_tanh(y[u]);
+          for (int i = 0; i < 8; ++i) {
+            y[i] = fmaf(__uint_as_float(r[g8 * 8 + i]), alpha[i], bias[i]);
+            if constexpr (kEpi == kGeluErf) y[i] = gelu_erf(y[i]);
+            if constexpr (kEpi == kGeluTanh) y[i] = gelu_tanh(y[i]);
+          }
           if constexpr (kEpi == kGated) {
             // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
-            const float g = __bfloat162float(p.gate[grow * p.ldg + n]);
-            const float res = __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + n]);
-            y[u] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[u]), g)), res);
-          }
-        }
-        w[e / 2] = pack_bf16x2(y[0], y[1]);
-      }
-      __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
-      if (nb + 32 <= p.N) {
-        uint4* d4 = reinterpret_cast<uint4*>(dst);
+            float gt[8], res[8];
+            unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.ldg + n)), gt);
+            unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(m) * p.ldr + n)), res);
 #pragma unroll
-        for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
-      } else {
-        const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
-        for (int e = 0; e < p.N - nb; ++e) dst[e] = wb[e];
+            for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[i]), gt[i])), res[i]);
+          }
+          reinterpret_cast<uint4*>(dst)[g8] =
+              make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                         pack_bf16x2(y[6], y[7]));
+        }
+      } else if (row_ok && nb < p.N) {
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float y[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int n = min(nb + e + u, p.N - 1);
+            const float alpha = sa * p.sb[n * p.sb_stride];
+            const float bias = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+            y[u] = fmaf(__uint_as_float(r[e + u]), alpha, bias);
+            if constexpr (kEpi == kGeluErf) y[u] = gelu_erf(y[u]);
+            if constexpr (kEpi == kGeluTanh) y[u] = gelu_tanh(y[u]);
+            if constexpr (kEpi == kGated) {
+              // reference: attn = bf16(GEMM); x = bf16(bf16(attn*gate) + res)
+              const float g = __bfloat162float(p.gate[grow * p.ldg + n]);
+              const float res = __bfloat162float(p.residual[static_cast<int64_t>(m) * p.ldr + n]);
+              y[u] = __fadd_rn(bf16_round(__fmul_rn(bf16_round(y[u]), g)), res);
+            }
+          }
+          w[e / 2] = pack_bf16x2(y[0], y[1]);
+        }
+        __nv_bfloat16* dst = p.out + static_cast<int64_t>(m) * p.ldo + nb;
+        if (nb + 32 <= p.N) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) d4[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+        } else {
+          const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+          for (int e = 0; e < p.N - nb; ++e) dst[e] = wb[e];
+        }
       }
     }
-  }
   }
 }
 

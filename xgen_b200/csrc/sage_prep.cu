@@ -122,15 +122,31 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const T* __restrict__ k
   }
 }
 
-__global__ void __launch_bounds__(kD) finalize_kernel(Workspace w, int64_t chunks, int64_t seq,
-                                                      float* __restrict__ v_scale) {
+// Per head: K channel means from the chunk partials and the V channel
+// scales. Eight slices of 128 threads each sum every eighth chunk, then the
+// slices are added in a fixed order (deterministic; 1,024 threads per head
+// instead of one serial pass per channel).
+constexpr int kFinalSlices = 8;
+
+__global__ void __launch_bounds__(kD* kFinalSlices) finalize_kernel(Workspace w, int64_t chunks,
+                                                                    int64_t seq,
+                                                                    float* __restrict__ v_scale) {
   const int64_t bh = blockIdx.x;
-  const int c = threadIdx.x;
+  const int c = threadIdx.x % kD;
+  const int slice = threadIdx.x / kD;
+  __shared__ float part[kFinalSlices][kD];
   float sum = 0.f;
-  for (int64_t i = 0; i < chunks; ++i) sum += w.ksum[(bh * chunks + i) * kD + c];
-  w.kmean[bh * kD + c] = __fdiv_rn(sum, static_cast<float>(seq));
-  const float s = __fdiv_rn(__int_as_float(w.vmax[bh * kD + c]), 448.0f);
-  v_scale[bh * kD + c] = fmaxf(s, FLT_MIN);
+  for (int64_t i = slice; i < chunks; i += kFinalSlices) sum += w.ksum[(bh * chunks + i) * kD + c];
+  part[slice][c] = sum;
+  __syncthreads();
+  if (slice == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < kFinalSlices; ++j) t += part[j][c];
+    w.kmean[bh * kD + c] = __fdiv_rn(t, static_cast<float>(seq));
+    const float sc = __fdiv_rn(__int_as_float(w.vmax[bh * kD + c]), 448.0f);
+    v_scale[bh * kD + c] = fmaxf(sc, FLT_MIN);
+  }
 }
 
 // Block abs-max over the CTA (kN threads).
@@ -158,8 +174,11 @@ __device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, cons
       uint32_t word = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int code = __float2int_rn(div_by(x[i][half * 4 + j], s, y));
-        word |= (static_cast<uint32_t>(max(-127, min(127, code))) & 0xFFu) << (8 * j);
+        // clamp to +-127, then round to nearest even by adding 1.5 * 2^23:
+        // the low byte of the sum's bits is the two's-complement code (the
+        // same code as rounding first and clamping after; NaN gives -127)
+        const float q = fminf(fmaxf(div_by(x[i][half * 4 + j], s, y), -127.0f), 127.0f);
+        word |= (__float_as_uint(__fadd_rn(q, 12582912.0f)) & 0xFFu) << (8 * j);
       }
       w[half] = word;
     }
@@ -321,7 +340,7 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
     auto kb = static_cast<const __nv_bfloat16*>(k);
     auto vb = static_cast<const __nv_bfloat16*>(v);
     stats_kernel<<<sgrid, kThreads, 0, st>>>(kb, ks, vb, vs, heads, seq, w, chunks);
-    finalize_kernel<<<static_cast<unsigned>(bh), kD, 0, st>>>(w, chunks, seq, v_scale);
+    finalize_kernel<<<static_cast<unsigned>(bh), kD * kFinalSlices, 0, st>>>(w, chunks, seq, v_scale);
     quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(qb, qs, kb, ks, vb, vs, heads, seq, s_pad, q_mult,
                                               w, v_scale, q8, q_scale, k8, k_scale, v8);
   } else {
@@ -329,7 +348,7 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
     auto kh = static_cast<const __half*>(k);
     auto vh = static_cast<const __half*>(v);
     stats_kernel<<<sgrid, kThreads, 0, st>>>(kh, ks, vh, vs, heads, seq, w, chunks);
-    finalize_kernel<<<static_cast<unsigned>(bh), kD, 0, st>>>(w, chunks, seq, v_scale);
+    finalize_kernel<<<static_cast<unsigned>(bh), kD * kFinalSlices, 0, st>>>(w, chunks, seq, v_scale);
     quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(qh, qs, kh, ks, vh, vs, heads, seq, s_pad, q_mult,
                                               w, v_scale, q8, q_scale, k8, k_scale, v8);
   }
