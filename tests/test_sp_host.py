@@ -141,3 +141,12 @@ def test_two_rank_sp_matches_single_rank(s, heads):
         uly, ph = results[r]
         assert torch.equal(uly, expect)
         assert torch.equal(ph, expect)
+
+
+def test_tail_split_switch(monkeypatch):
+    """XGB_ATTN_TAIL_SPLIT=0 hands the attention kernels no split workspace
+    (so they run unsplit); the lookup happens before any device work."""
+    from xgen_b200 import attention
+
+    monkeypatch.setenv("XGB_ATTN_TAIL_SPLIT", "0")
+    assert attention._ws_args(torch.device("cuda", 0)) == (None, 0)
