@@ -103,3 +103,34 @@ def test_output_adaln_matches_layernorm_then_indexed_affine(cuda_device):
         bound = (n.float() * f).abs() * 2 ** -7 + eager.float().abs() * 2 ** -7 + 1e-6
         assert (fused == eager).float().mean() > 0.99
         assert ((fused.float() - eager.float()).abs() <= bound).all()
+
+
+@pytest.mark.parametrize("norm,h", [("rmsnorm", 1536), ("rmsnorm", 5376), ("layernorm", 4096),
+                                    ("layernorm", 512), ("rmsnorm", 1004)])
+def test_norm_modulate_quant_widths(cuda_device, norm, h):
+    """The fused prologue for RMSNorm x weight and LayerNorm at widths that
+    take each vector variant (1-6 chunks per thread) and the scalar kernel
+    (h % 8 != 0): within one bf16 ulp of torch's norm + the bit-exact
+    indexed affine, and its e4m3 codes equal per-token quantisation of its
+    own bf16 output."""
+    from xgen_b200.ops import indexed_affine, norm_modulate_quant, quantize_per_token
+
+    g = torch.Generator().manual_seed(h)
+    b, s = 1, 96
+    x = (2 * torch.randn(b, s, h, generator=g)).bfloat16().to(cuda_device)
+    table = torch.randn(3, 2 * h, generator=g).bfloat16().to(cuda_device)
+    shift, scale = table[:, :h], table[:, h:]
+    idx = torch.randint(3, (s,), generator=g).to(cuda_device)
+    w = (1 + 0.1 * torch.randn(h, generator=g)).bfloat16().to(cuda_device) if norm == "rmsnorm" else None
+    codes, scales, mod = norm_modulate_quant(x, norm, w, 1e-6, scale, shift, idx, return_bf16=True)
+    if norm == "rmsnorm":
+        n = torch.nn.functional.rms_norm(x.float(), (h,), w.float(), eps=1e-6).bfloat16()
+    else:
+        n = torch.nn.functional.layer_norm(x.float(), (h,), eps=1e-6).bfloat16()
+    ref_mod = indexed_affine(n, scale, shift, idx, modulation=True)
+    f = (1.0 + scale.index_select(0, idx).float()).bfloat16().float()
+    bound = (n.float() * f).abs() * 2 ** -7 + ref_mod.float().abs() * 2 ** -7 + 1e-6
+    assert (mod == ref_mod).float().mean() > 0.99
+    assert ((mod.float() - ref_mod.float()).abs() <= bound).all()
+    rc, rs = quantize_per_token(mod.reshape(b * s, h))
+    assert torch.equal(scales, rs) and torch.equal(codes.view(torch.uint8), rc.view(torch.uint8))
