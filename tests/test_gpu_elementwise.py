@@ -220,3 +220,42 @@ def test_wire_encode_fused_rope_vs_oracle(cuda_device, peers, seq, batch, hpd, r
         srcs.append(x5)
     want = of.wire_encode(srcs, peers)
     assert np.array_equal(got.cpu().numpy(), want)
+
+
+def test_wire_encode_full_sp8_shard_vs_oracle(cuda_device):
+    """The bench's encode at full size: one SP8 rank's 768P-5s shard (15,856
+    tokens, 24 heads, 3 per peer, 3-D RoPE over all 128 channels), the last
+    8 rows beyond the real sequence (valid_seq), bit-exact against the
+    oracle's RoPE + wire encode; then decode reproduces the oracle's e4m3
+    round trip."""
+    from xgen_b200.h3.rope import rope_3d
+    from xgen_b200.phaa import fp8_transport as fp8
+    from xgen_b200.phaa.fp8_transport import WireView
+
+    peers, seq, heads = 8, 15856, 24
+    hpd = heads // peers
+    g = torch.Generator().manual_seed(8)
+    q, k, v = (torch.randn(1, seq, heads * 128, generator=g).bfloat16() for _ in range(3))
+    cos, sin = rope_3d((31, 48, 84), 512 + 1250)
+    cos, sin = cos[7 * seq:7 * seq + seq].contiguous(), sin[7 * seq:7 * seq + seq].contiguous()
+    cos = torch.cat([cos, torch.ones(seq - cos.shape[0], 128)])
+    sin = torch.cat([sin, torch.zeros(seq - sin.shape[0], 128)])
+    valid = peers * seq - 8
+    views = [t.to(cuda_device).unflatten(-1, (heads, 128)).unflatten(2, (peers, hpd)).permute(2, 1, 0, 3, 4)
+             for t in (q, k, v)]
+    wire = fp8.encode(views, 128, peers, rotary_emb=(cos.to(cuda_device), sin.to(cuda_device)),
+                      views=[WireView.of(x) for x in views], valid_seq=valid)
+    q4, k4, v4 = (t.float().numpy().reshape(1, seq, heads, 128) for t in (q, k, v))
+    qr, kr = ew.partial_rope(q4, k4, cos.numpy(), sin.numpy())
+    srcs = []
+    for x in (qr, kr, v4):
+        x5 = x.reshape(1, seq, peers, hpd, 128).transpose(2, 1, 0, 3, 4).copy()
+        x5[peers - 1, seq - 8:] = 0  # global index peer*seq + s >= valid
+        srcs.append(x5)
+    want = of.wire_encode(srcs, peers)
+    assert np.array_equal(wire.cpu().numpy(), want)
+    outs = [torch.empty(peers, seq, 1, hpd, 128, device=cuda_device, dtype=torch.bfloat16) for _ in range(3)]
+    fp8.decode(wire, outs, 128, peers)
+    back = of.wire_decode(want, 3, peers * seq * hpd, peers, 128)
+    for o, r in zip(outs, back):
+        assert np.array_equal(host_bits(o).reshape(-1), bf16_bits_from_f32(r.reshape(-1)))
