@@ -158,7 +158,7 @@ def hbm_kernels(args):
     import torch
 
     from xgen_b200 import ops
-    from xgen_b200.attention import SageWorkspace, kernel_errors, sage_prepare
+    from xgen_b200.attention import SageWorkspace, kernel_errors, sage_prepare, sage_prepare_wire
     from xgen_b200.h3.rope import rope_3d
     from xgen_b200.phaa import fp8_transport as wire
 
@@ -204,7 +204,13 @@ def hbm_kernels(args):
     gathered = [torch.empty(sp, s_loc, 1, hl, HEAD_DIM, device=dev, dtype=torch.bfloat16) for _ in range(3)]
     ms = timed(lambda: wire.decode(buf, gathered, HEAD_DIM, sp))
     record("fp8_wire_decode", payload + 3 * s_loc * width * 2, ms, f"-> 3 x [{sp}, {s_loc}, 1, {hl}, 128] bf16")
-    del qkv, buf
+    # the PHAA Sage path: Sage preparation reading the received wire itself
+    ws_wire = SageWorkspace(1, hl, SEQ, dev)
+    ms = timed(lambda: sage_prepare_wire(buf, peers=sp, seq=s_loc, batch=1, heads=hl, valid_seq=SEQ, ws=ws_wire))
+    n = hl * SEQ * HEAD_DIM
+    record("sage_prep_from_wire", payload + 3 * n + (2 * ws_wire.q_scale.numel() + ws_wire.v_scale.numel()) * 4,
+           ms, f"wire of 3 x [{sp}, {s_loc}, 1, {hl}] rows -> Sage operands (replaces decode + sage_prep)")
+    del qkv, buf, ws_wire
 
     # Sage preparation on the gathered layout (strided [B, H, S_real, D] views)
     views = [t.permute(2, 3, 0, 1, 4).flatten(2, 3)[:, :, :SEQ] for t in gathered]

@@ -259,6 +259,20 @@ int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void* k,
                      int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
                      float* v_scale, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* xgb_sage_prepare reading Q/K/V straight from a received PHAA FP8 wire
+ * (the payload fp8_all_to_all_many exchanges, x_base/x_base/phaa/
+ * fp8_transport.py:85-144, before its decode): per source peer p the Q, K
+ * and V sections of rows [s < seq, batch, head] (128 e4m3 bytes + fp32
+ * scale each), then peer_padding bytes. Attention row g < valid_seq is row
+ * g % seq of peer g / seq; each value is read as bf16(e4m3 * scale), the
+ * decode's result, so the outputs equal decode + xgb_sage_prepare on
+ * [batch, heads, valid_seq, 128]. workspace: xgb_sage_prepare_workspace(
+ * batch, heads, valid_seq) bytes; payload 4-byte aligned. */
+int xgb_sage_prepare_wire(const uint8_t* payload, int64_t peers, int64_t seq, int64_t batch,
+                          int64_t heads, int64_t valid_seq, int64_t peer_padding, float sm_scale,
+                          int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
+                          float* v_scale, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Non-causal attention over xgb_sage_prepare's outputs: INT8 Q.K^T
  * (tcgen05 kind::i8), fp32 online softmax in the exp2 domain, e4m3 P.V
  * (kind::f8f6f4), fp32 accumulation; writes bf16 out[b, h, s, :] at element

@@ -154,3 +154,27 @@ def test_tail_split_matches_unsplit(cuda_device, precision, h, s):
         assert oa.cosine(a, b) >= tol[0]
         assert np.abs(a - b).max() <= tol[1]
     assert torch.equal(parts[0], parts[1]) and torch.equal(parts[1], parts[2])
+
+
+@pytest.mark.parametrize("peers,seq,batch,heads,valid,padding",
+                         [(2, 150, 1, 3, 297, 0), (4, 64, 2, 2, 256, 12), (8, 1000, 1, 3, 7990, 4)])
+def test_sage_prepare_from_wire_equals_decode(cuda_device, peers, seq, batch, heads, valid, padding):
+    """xgb_sage_prepare_wire on a PHAA FP8 wire gives the same Sage operands
+    as decoding the wire to bf16 and preparing from [batch, heads, valid,
+    128] views: every code and scale equal."""
+    from xgen_b200.attention import sage_prepare, sage_prepare_wire
+    from xgen_b200.phaa import fp8_transport as fp8
+
+    g = torch.Generator(device=cuda_device).manual_seed(seq + heads)
+    shape = (peers, seq, batch, heads, 128)
+    q, k, v = (torch.randn(shape, device=cuda_device, generator=g).bfloat16() for _ in range(3))
+    k = (k.float() + 2.0).bfloat16()
+    wire = fp8.encode([q, k, v], 128, peers, peer_padding=padding)
+    outs = [torch.empty(shape, device=cuda_device, dtype=torch.bfloat16) for _ in range(3)]
+    fp8.decode(wire, outs, 128, peers, peer_padding=padding)
+    views = [x.permute(2, 3, 0, 1, 4).flatten(2, 3)[:, :, :valid] for x in outs]
+    a = sage_prepare(*views)
+    b = sage_prepare_wire(wire, peers=peers, seq=seq, batch=batch, heads=heads, valid_seq=valid,
+                          peer_padding=padding)
+    for name in ("q8", "q_scale", "k8", "k_scale", "v8", "v_scale"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), name

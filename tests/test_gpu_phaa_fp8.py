@@ -177,3 +177,43 @@ def test_async_variants_with_b200_attention(cuda_device):
     for name in ("tail", "async", "direct", "tiled", "packed", "direct_qkv", "all_direct"):
         assert torch.equal(r["natural"], r[name]), name
     assert backend.kernel_calls > 0
+
+
+@pytest.mark.parametrize("fuse_rope", [False, True])
+def test_sage_from_wire_matches_decode_path(cuda_device, fuse_rope):
+    """With a Sage backend, PHAA prepares Q/K/V straight from the received
+    FP8 wire (sage_prepare_wire): bit-identical to decoding the wire into
+    bf16 gather buffers and calling the same backend on them, with the SP
+    pad row and (optionally) the fused pre-A2A RoPE."""
+    from xgen_b200.attention import H3AttentionBackendB200
+    from xgen_b200.phaa import phaa_attention
+
+    backend = H3AttentionBackendB200("sage")
+
+    class ViaDecode:  # hides `precision`: PHAA decodes into gather buffers
+        writes_into = True
+
+        def __call__(self, q, k, v, **kw):
+            return backend(q, k, v, **kw)
+
+    g = torch.Generator(device=cuda_device).manual_seed(21)
+    qkv = [torch.randn((1, 301, 8 * 128), dtype=torch.bfloat16, device=cuda_device, generator=g)
+           for _ in range(3)]
+    ang = torch.rand(301, 48, device=cuda_device, generator=g) * 3
+    rot = (torch.cat([ang.cos(), ang.cos()], -1).float().contiguous(),
+           torch.cat([ang.sin(), ang.sin()], -1).float().contiguous())
+    options = dict(comm_stream=torch.cuda.Stream(), sp_group=None, sp_size=2, heads=8,
+                   phaa_split_num=2, head_dim=128, fp8_transport=True,
+                   rotary_emb=rot if fuse_rope else None, fuse_rope=fuse_rope)
+    get_pad_manager()._pads["pad"] = 1
+    try:
+        with patch.object(dist, "get_world_size", return_value=2), \
+             patch.object(dist, "all_to_all_single", side_effect=_Async()):
+            before = backend.kernel_calls
+            wire = phaa_attention.run_phaa_attention(*qkv, attention_fn=backend, **options)
+            assert backend.kernel_calls - before == 2
+            decoded = phaa_attention.run_phaa_attention(*qkv, attention_fn=ViaDecode(), **options)
+        torch.cuda.synchronize()
+    finally:
+        get_pad_manager().clear()
+    assert torch.equal(wire, decoded)

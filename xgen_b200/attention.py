@@ -122,6 +122,28 @@ def sage_prepare(q, k, v, sm_scale: float | None = None, ws: SageWorkspace | Non
     return ws
 
 
+def sage_prepare_wire(wire: torch.Tensor, *, peers: int, seq: int, batch: int, heads: int,
+                      valid_seq: int, peer_padding: int = 0, sm_scale: float | None = None,
+                      ws: SageWorkspace | None = None) -> SageWorkspace:
+    """sage_prepare on Q/K/V read straight from a received PHAA FP8 wire
+    (uint8, peer-major [Q|K|V] sections of rows [seq, batch, heads] per
+    peer): the same outputs as decoding the wire into bf16 [batch, heads,
+    valid_seq, 128] and calling sage_prepare, without the decode pass."""
+    if wire.dtype != torch.uint8 or not wire.is_cuda or not wire.is_contiguous():
+        raise ValueError("Sage wire preparation needs a contiguous CUDA uint8 wire")
+    expect = peers * (3 * seq * batch * heads * (HEAD_DIM + 4) + peer_padding)
+    if wire.numel() != expect:
+        raise ValueError("PHAA FP8 wire size does not match its layout")
+    sm_scale = float(sm_scale) if sm_scale is not None else 1.0 / math.sqrt(HEAD_DIM)
+    if ws is None or ws.shape != (batch, heads, valid_seq):
+        ws = SageWorkspace(batch, heads, valid_seq, wire.device)
+    call("xgb_sage_prepare_wire", wire.data_ptr(), peers, seq, batch, heads, valid_seq, peer_padding,
+         sm_scale, ws.q8.data_ptr(), ws.q_scale.data_ptr(), ws.k8.data_ptr(), ws.k_scale.data_ptr(),
+         ws.v8.data_ptr(), ws.v_scale.data_ptr(), ws.scratch.data_ptr(), ws.scratch_bytes,
+         torch.cuda.current_stream(wire.device).cuda_stream)
+    return ws
+
+
 def sage_attention_prepared(ws: SageWorkspace, out: torch.Tensor | None = None) -> torch.Tensor:
     """The tcgen05 INT8-QK / FP8-PV attention over a prepared workspace."""
     b, h, s = ws.shape
@@ -183,6 +205,24 @@ class H3AttentionBackendB200:
                 and key.dtype == query.dtype and value.dtype == query.dtype
                 and all(t.stride(-1) == 1 for t in (query, key, value))
                 and (self.precision == "bf16" or query.shape == key.shape))
+
+    def attend_fp8_wire(self, wire, *, peers, seq, batch, heads, valid_seq, peer_padding=0, out):
+        """Sage attention on Q/K/V read straight from a received PHAA FP8
+        wire (sage_prepare_wire): the same result as decoding the wire and
+        calling this backend on [batch, heads, valid_seq, 128] views. out is
+        a bf16 (batch, heads, valid_seq, 128) view."""
+        if self.precision != "sage":
+            raise ValueError("attention from the FP8 wire is the Sage path")
+        key_ = ("wire", batch, heads, valid_seq, wire.device)
+        if self._ws is None:
+            self._ws = {}
+        ws = sage_prepare_wire(wire, peers=peers, seq=seq, batch=batch, heads=heads, valid_seq=valid_seq,
+                               peer_padding=peer_padding, ws=self._ws.get(key_))
+        self._ws[key_] = ws
+        sage_attention_prepared(ws, out)
+        self.kernel_calls += 1
+        self.calls += 1
+        return out
 
     def __call__(self, query, key, value, *, attn_mask=None, head_offset=0, out=None):
         if self._kernel_eligible(query, key, value, attn_mask) and (

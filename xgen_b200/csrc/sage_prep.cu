@@ -64,17 +64,66 @@ __device__ __forceinline__ void unpack8(const uint4& raw, float (&x)[8]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) x[j] = tf<T>(e[j]);
 }
+
+// Where the kernels read Q (stream 0), K (1) and V (2) rows of 128 channels
+// of (batch b, head h, sequence row): `load` fetches the 8 channels from c0
+// in a raw form, `unpack` turns them into fp32.
+//
+// StridedSource: bf16/fp16 [B, H, S, 128] views with element strides.
 template <typename T>
-__device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
-  unpack8<T>(__ldg(reinterpret_cast<const uint4*>(p)), x);
-}
+struct StridedSource {
+  const T* p[3];
+  Strides st[3];
+  using Raw = uint4;
+  __device__ __forceinline__ Raw load(int stream, int64_t b, int64_t h, int64_t row, int c0) const {
+    return __ldg(reinterpret_cast<const uint4*>(p[stream] + b * st[stream].b + h * st[stream].h +
+                                                row * st[stream].s + c0));
+  }
+  __device__ __forceinline__ static Raw zero() { return make_uint4(0, 0, 0, 0); }
+  __device__ __forceinline__ static void unpack(const Raw& r, float (&x)[8]) { unpack8<T>(r, x); }
+};
+
+// WireSource: the received PHAA FP8 wire (x_base/x_base/phaa/fp8_transport.py
+// :26-63): per source peer p, the Q, K and V sections of its rows
+// [s, batch, head] (s < seq, the peer's shard), each row 128 e4m3 bytes and
+// an fp32 scale. Sequence row g of the attention is row g % seq of peer
+// g / seq. A value reads as bf16(e4m3 * scale), the wire decode's result,
+// so the prepared operands equal those of decode + StridedSource.
+struct WireSource {
+  const uint8_t* payload;
+  int64_t batch, heads, peer_rows, peer_bytes;
+  FastDiv div_seq;
+  struct Raw {
+    uint32_t lo, hi;
+    float scale;
+  };
+  __device__ __forceinline__ Raw load(int stream, int64_t b, int64_t h, int64_t row, int c0) const {
+    const uint32_t peer = fast_div(static_cast<uint32_t>(row), div_seq);
+    const int64_t s = row - static_cast<int64_t>(peer) * div_seq.d;
+    const uint8_t* r = payload + peer * peer_bytes +
+                       (stream * peer_rows + (s * batch + b) * heads + h) * (kD + 4);
+    return Raw{__ldg(reinterpret_cast<const uint32_t*>(r + c0)),
+               __ldg(reinterpret_cast<const uint32_t*>(r + c0 + 4)),
+               __ldg(reinterpret_cast<const float*>(r + kD))};
+  }
+  __device__ __forceinline__ static Raw zero() { return Raw{0, 0, 0.f}; }
+  __device__ __forceinline__ static void unpack(const Raw& r, float (&x)[8]) {
+    const uint32_t w[2] = {r.lo, r.hi};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint16_t pair = static_cast<uint16_t>(w[k / 2] >> (16 * (k & 1)));
+      const float2 f = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3)));
+      const uint32_t b2 = round_bf16x2(__fmul_rn(f.x, r.scale), __fmul_rn(f.y, r.scale));
+      x[2 * k] = __uint_as_float(b2 << 16);
+      x[2 * k + 1] = __uint_as_float(b2 & 0xFFFF0000u);
+    }
+  }
+};
 
 // Per 512-row chunk of one head: channel sums of K and channel abs-max of V.
-// Thread t owns channels 8*(t%16)..+8 of rows t/16 + 16*i (16-byte loads).
-template <typename T>
-__global__ void __launch_bounds__(kThreads) stats_kernel(const T* __restrict__ k, Strides ks,
-                                                         const T* __restrict__ v, Strides vs,
-                                                         int64_t heads, int64_t seq,
+// Thread t owns channels 8*(t%16)..+8 of rows t/16 + 16*i.
+template <typename Src>
+__global__ void __launch_bounds__(kThreads) stats_kernel(Src src, int64_t heads, int64_t seq,
                                                          Workspace w, int64_t chunks) {
   const int64_t bh = blockIdx.y;
   const int64_t b = bh / heads, h = bh % heads;
@@ -83,8 +132,6 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const T* __restrict__ k
   const int c0 = cg * 8;
   const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * kStatsRows;
   const int64_t row_end = min(row_begin + kStatsRows, seq);
-  const T* kp = k + b * ks.b + h * ks.h + c0;
-  const T* vp = v + b * vs.b + h * vs.h + c0;
   float sum[8], vmx[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -93,8 +140,8 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(const T* __restrict__ k
   }
   for (int64_t r = row_begin + rr; r < row_end; r += kThreads / 16) {
     float kx[8], vx[8];
-    load8<T>(kp + r * ks.s, kx);
-    load8<T>(vp + r * vs.s, vx);
+    Src::unpack(src.load(1, b, h, r, c0), kx);
+    Src::unpack(src.load(2, b, h, r, c0), vx);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       sum[j] += kx[j];
@@ -193,13 +240,11 @@ __device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, cons
 constexpr int kQuantThreads = 512;
 constexpr int kQuantRows = 64 * 16 / kQuantThreads;  // rows per thread
 
-template <typename T>
+template <typename Src>
 __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
-    const T* __restrict__ q, Strides qs, const T* __restrict__ k, Strides ks,
-    const T* __restrict__ v, Strides vs, int64_t heads, int64_t seq, int64_t s_pad,
-    float q_mult, Workspace w, const float* __restrict__ v_scale, int8_t* __restrict__ q8,
-    float* __restrict__ q_scale, int8_t* __restrict__ k8, float* __restrict__ k_scale,
-    uint8_t* __restrict__ v8) {
+    Src src, int64_t heads, int64_t seq, int64_t s_pad, float q_mult, Workspace w,
+    const float* __restrict__ v_scale, int8_t* __restrict__ q8, float* __restrict__ q_scale,
+    int8_t* __restrict__ k8, float* __restrict__ k_scale, uint8_t* __restrict__ v8) {
   const int64_t bh = blockIdx.y;
   const int64_t b = bh / heads, h = bh % heads;
   const int64_t blk = blockIdx.x;
@@ -212,15 +257,14 @@ __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
   constexpr int kStep = 64 / R;
   __shared__ float red[kQuantThreads / 32];
   float x[R][8];
-  uint4 rq[R], rk[R], rv[R];
+  typename Src::Raw rq[R], rk[R], rv[R];
 #pragma unroll
   for (int i = 0; i < R; ++i) {
     const int64_t row = row0 + kStep * i;
     const bool ok = row < seq;
-    const uint4 zero = make_uint4(0, 0, 0, 0);
-    rq[i] = ok ? __ldg(reinterpret_cast<const uint4*>(q + b * qs.b + h * qs.h + row * qs.s + c0)) : zero;
-    rk[i] = ok ? __ldg(reinterpret_cast<const uint4*>(k + b * ks.b + h * ks.h + row * ks.s + c0)) : zero;
-    rv[i] = ok ? __ldg(reinterpret_cast<const uint4*>(v + b * vs.b + h * vs.h + row * vs.s + c0)) : zero;
+    rq[i] = ok ? src.load(0, b, h, row, c0) : Src::zero();
+    rk[i] = ok ? src.load(1, b, h, row, c0) : Src::zero();
+    rv[i] = ok ? src.load(2, b, h, row, c0) : Src::zero();
   }
 
   // Values are recomputed from the raw words in each pass (the same
@@ -233,7 +277,7 @@ __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
   float a = 0.f;
 #pragma unroll
   for (int i = 0; i < R; ++i) {
-    unpack8<T>(rq[i], x[i]);
+    Src::unpack(rq[i], x[i]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(__fmul_rn(x[i][j], q_mult)));
   }
@@ -242,7 +286,7 @@ __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
   if (threadIdx.x == 0) q_scale[bh * (s_pad / 64) + blk] = sc;
 #pragma unroll
   for (int i = 0; i < R; ++i) {
-    unpack8<T>(rq[i], x[i]);
+    Src::unpack(rq[i], x[i]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[i][j] = __fmul_rn(x[i][j], q_mult);  // rows >= seq: 0
   }
@@ -255,7 +299,7 @@ __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
   a = 0.f;
 #pragma unroll
   for (int i = 0; i < R; ++i) {
-    unpack8<T>(rk[i], x[i]);
+    Src::unpack(rk[i], x[i]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) a = fmaxf(a, ok[i] ? fabsf(__fsub_rn(x[i][j], mean[j])) : 0.f);
   }
@@ -264,7 +308,7 @@ __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
   if (threadIdx.x == 0) k_scale[bh * (s_pad / 64) + blk] = sc;
 #pragma unroll
   for (int i = 0; i < R; ++i) {
-    unpack8<T>(rk[i], x[i]);
+    Src::unpack(rk[i], x[i]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[i][j] = ok[i] ? __fsub_rn(x[i][j], mean[j]) : 0.f;
   }
@@ -279,13 +323,45 @@ __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
   }
 #pragma unroll
   for (int i = 0; i < R; ++i) {
-    unpack8<T>(rv[i], x[i]);
+    Src::unpack(rv[i], x[i]);
     uint32_t q[4];
 #pragma unroll
     for (int j = 0; j < 8; j += 2)
       q[j / 2] = e4m3x2(div_by(x[i][j], vsc[j], vrc[j]), div_by(x[i][j + 1], vsc[j + 1], vrc[j + 1]));
     *reinterpret_cast<uint2*>(v8 + off0 + kStep * i * kD) = make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
   }
+}
+
+struct Outputs {
+  int8_t* q8;
+  float* q_scale;
+  int8_t* k8;
+  float* k_scale;
+  uint8_t* v8;
+  float* v_scale;
+};
+
+inline int64_t stats_workspace(int64_t bh, int64_t seq) {
+  return bh * stats_chunks(seq) * kD * 4 + bh * kD * 4 + bh * kD * 4;
+}
+
+// Statistics, finalize and quantisation of [batch, heads, seq] rows read from `src`.
+template <typename Src>
+int prepare(const Src& src, int64_t batch, int64_t heads, int64_t seq, float sm_scale,
+            const Outputs& o, void* workspace, cudaStream_t st) {
+  const int64_t bh = batch * heads;
+  const int64_t chunks = stats_chunks(seq);
+  const int64_t s_pad = (seq + 127) / 128 * 128;
+  Workspace w = carve(workspace, bh, chunks);
+  if (cudaMemsetAsync(w.vmax, 0, bh * kD * sizeof(int), st) != cudaSuccess) return XGB_ERR_LAUNCH;
+  const float q_mult = sm_scale * kLog2e;
+  const dim3 sgrid(static_cast<unsigned>(chunks), static_cast<unsigned>(bh));
+  const dim3 qgrid(static_cast<unsigned>(s_pad / 64), static_cast<unsigned>(bh));
+  stats_kernel<<<sgrid, kThreads, 0, st>>>(src, heads, seq, w, chunks);
+  finalize_kernel<<<static_cast<unsigned>(bh), kD * kFinalSlices, 0, st>>>(w, chunks, seq, o.v_scale);
+  quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(src, heads, seq, s_pad, q_mult, w, o.v_scale, o.q8,
+                                                o.q_scale, o.k8, o.k_scale, o.v8);
+  return launch_status();
 }
 
 }  // namespace
@@ -295,8 +371,7 @@ using namespace xgb;
 
 XGB_API int64_t xgb_sage_prepare_workspace(int64_t batch, int64_t heads, int64_t seq) {
   if (batch <= 0 || heads <= 0 || seq <= 0) return 0;
-  const int64_t bh = batch * heads;
-  return bh * stats_chunks(seq) * kD * 4 + bh * kD * 4 + bh * kD * 4;
+  return stats_workspace(batch * heads, seq);
 }
 
 XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void* k,
@@ -323,34 +398,46 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
     return XGB_ERR_ALIGN;
   const int64_t need = xgb_sage_prepare_workspace(batch, heads, seq);
   if (!workspace || workspace_bytes < need) return XGB_ERR_WORKSPACE;
-  const int64_t bh = batch * heads;
-  const int64_t chunks = stats_chunks(seq);
-  const int64_t s_pad = (seq + 127) / 128 * 128;
-  Workspace w = carve(workspace, bh, chunks);
-  cudaStream_t st = as_stream(stream);
-  if (cudaMemsetAsync(w.vmax, 0, bh * kD * sizeof(int), st) != cudaSuccess) return XGB_ERR_LAUNCH;
   const Strides qs{q_strides[0], q_strides[1], q_strides[2]};
   const Strides ks{k_strides[0], k_strides[1], k_strides[2]};
   const Strides vs{v_strides[0], v_strides[1], v_strides[2]};
-  const float q_mult = sm_scale * kLog2e;
-  dim3 sgrid(static_cast<unsigned>(chunks), static_cast<unsigned>(bh));
-  dim3 qgrid(static_cast<unsigned>(s_pad / 64), static_cast<unsigned>(bh));
+  const Outputs o{q8, q_scale, k8, k_scale, v8, v_scale};
   if (dtype == XGB_BF16) {
-    auto qb = static_cast<const __nv_bfloat16*>(q);
-    auto kb = static_cast<const __nv_bfloat16*>(k);
-    auto vb = static_cast<const __nv_bfloat16*>(v);
-    stats_kernel<<<sgrid, kThreads, 0, st>>>(kb, ks, vb, vs, heads, seq, w, chunks);
-    finalize_kernel<<<static_cast<unsigned>(bh), kD * kFinalSlices, 0, st>>>(w, chunks, seq, v_scale);
-    quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(qb, qs, kb, ks, vb, vs, heads, seq, s_pad, q_mult,
-                                              w, v_scale, q8, q_scale, k8, k_scale, v8);
-  } else {
-    auto qh = static_cast<const __half*>(q);
-    auto kh = static_cast<const __half*>(k);
-    auto vh = static_cast<const __half*>(v);
-    stats_kernel<<<sgrid, kThreads, 0, st>>>(kh, ks, vh, vs, heads, seq, w, chunks);
-    finalize_kernel<<<static_cast<unsigned>(bh), kD * kFinalSlices, 0, st>>>(w, chunks, seq, v_scale);
-    quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(qh, qs, kh, ks, vh, vs, heads, seq, s_pad, q_mult,
-                                              w, v_scale, q8, q_scale, k8, k_scale, v8);
+    using S = StridedSource<__nv_bfloat16>;
+    const S src{{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                 static_cast<const __nv_bfloat16*>(v)}, {qs, ks, vs}};
+    return prepare(src, batch, heads, seq, sm_scale, o, workspace, as_stream(stream));
   }
-  return launch_status();
+  using S = StridedSource<__half>;
+  const S src{{static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v)},
+              {qs, ks, vs}};
+  return prepare(src, batch, heads, seq, sm_scale, o, workspace, as_stream(stream));
+}
+
+XGB_API int xgb_sage_prepare_wire(const uint8_t* payload, int64_t peers, int64_t seq,
+                                  int64_t batch, int64_t heads, int64_t valid_seq,
+                                  int64_t peer_padding, float sm_scale, int8_t* q8, float* q_scale,
+                                  int8_t* k8, float* k_scale, uint8_t* v8, float* v_scale,
+                                  void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!payload || !q8 || !q_scale || !k8 || !k_scale || !v8 || !v_scale) return XGB_ERR_ARG;
+  if (peers <= 0 || seq <= 0 || batch <= 0 || heads <= 0) return XGB_ERR_SHAPE;
+  if (valid_seq <= 0 || valid_seq > peers * seq || peers * seq > INT32_MAX) return XGB_ERR_SHAPE;
+  if (peer_padding < 0 || peer_padding % 4) return XGB_ERR_ARG;
+  if (!(sm_scale > 0.f)) return XGB_ERR_ARG;
+  // 4-byte loads of codes and scales: the wire rows start at 4-byte multiples
+  if ((reinterpret_cast<uintptr_t>(payload) & 3u) ||
+      ((reinterpret_cast<uintptr_t>(q8) | reinterpret_cast<uintptr_t>(k8) |
+        reinterpret_cast<uintptr_t>(v8)) & 15u))
+    return XGB_ERR_ALIGN;
+  const int64_t need = xgb_sage_prepare_workspace(batch, heads, valid_seq);
+  if (!workspace || workspace_bytes < need) return XGB_ERR_WORKSPACE;
+  WireSource src{};
+  src.payload = payload;
+  src.batch = batch;
+  src.heads = heads;
+  src.peer_rows = seq * batch * heads;
+  src.peer_bytes = 3 * src.peer_rows * (kD + 4) + peer_padding;
+  src.div_seq = make_fastdiv(static_cast<uint32_t>(seq));
+  const Outputs o{q8, q_scale, k8, k_scale, v8, v_scale};
+  return prepare(src, batch, heads, valid_seq, sm_scale, o, workspace, as_stream(stream));
 }

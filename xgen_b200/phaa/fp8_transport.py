@@ -136,14 +136,32 @@ def fp8_all_to_all_many(outputs, tensors, head_dim, group, *, rotary_emb=None):
     streams = len(tensors)
     if streams not in (1, 3) or len(outputs) != streams:
         raise ValueError("PHAA FP8 transport expects one tensor or a QKV triple")
-    if any(t.device.type != "cuda" for t in (*outputs, *tensors)):
+    if any(t.device.type != "cuda" for t in outputs):
         raise ValueError("PHAA FP8 transport requires CUDA tensors")
-    shape = tensors[0].shape
-    if head_dim % 4 or any(x.shape != shape for x in (*outputs, *tensors)):
+    if any(x.shape != tensors[0].shape for x in outputs):
         raise ValueError("PHAA FP8 transport requires matching shapes and head dim divisible by four")
     if any(not out.is_contiguous() for out in outputs):
         raise ValueError("PHAA FP8 transport requires contiguous outputs")
-    if any(t.dtype not in _DTYPE for t in (*outputs, *tensors)):
+    if any(t.dtype not in _DTYPE for t in outputs):
+        raise ValueError("PHAA FP8 transport requires bf16/fp16 tensors")
+    recv, peers, peer_padding = fp8_exchange_wire(tensors, head_dim, group, rotary_emb=rotary_emb)
+    decode(recv, outputs, head_dim, peers, peer_padding=peer_padding)
+
+
+def fp8_exchange_wire(tensors, head_dim, group, *, rotary_emb=None):
+    """Encode and exchange, without the decode: returns (received wire as
+    uint8 [bytes], peers, peer_padding) for a consumer that reads the wire
+    itself (sage_prepare_wire). The received wire is allocated on the
+    current stream."""
+    streams = len(tensors)
+    if streams not in (1, 3):
+        raise ValueError("PHAA FP8 transport expects one tensor or a QKV triple")
+    if any(t.device.type != "cuda" for t in tensors):
+        raise ValueError("PHAA FP8 transport requires CUDA tensors")
+    shape = tensors[0].shape
+    if head_dim % 4 or any(x.shape != shape for x in tensors):
+        raise ValueError("PHAA FP8 transport requires matching shapes and head dim divisible by four")
+    if any(t.dtype not in _DTYPE for t in tensors):
         raise ValueError("PHAA FP8 transport requires bf16/fp16 tensors")
     rows = tensors[0].numel() // head_dim
     peers = dist.get_world_size(group)
@@ -169,4 +187,4 @@ def fp8_all_to_all_many(outputs, tensors, head_dim, group, *, rotary_emb=None):
     send = send.view(wire_shape)
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)
-    decode(recv, outputs, head_dim, peers, peer_padding=peer_padding)
+    return recv.view(-1), peers, peer_padding

@@ -136,8 +136,17 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             return (B, cs, W_S * Sq - pad, D)
         return (W_S, Sq, B, cs, D)
 
-    gather = [tuple(torch.empty(gather_shape(cs), device=query.device, dtype=query.dtype)
-                    for _ in range(3)) for cs in sizes]
+    # Sage backends take the received FP8 wire as it is: the Sage
+    # preparation reads Q/K/V from it (bf16(e4m3 * scale), the decode's
+    # values), so there is no decode pass and no bf16 gather buffer.
+    from_wire = (fp8_transport and not async_exchange and attention_mask is None
+                 and (rope_fn is None or rotary_emb is None or fuse_rope) and D == 128
+                 and getattr(attention_fn, "precision", None) == "sage"
+                 and hasattr(attention_fn, "attend_fp8_wire"))
+    wires = [None] * phaa_split_num
+    gather = [None if from_wire else
+              tuple(torch.empty(gather_shape(cs), device=query.device, dtype=query.dtype) for _ in range(3))
+              for cs in sizes]
     if direct_return:
         final = torch.empty((B, Sq, H), device=query.device, dtype=query.dtype)
         returned = None
@@ -159,7 +168,10 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             for t in chunks[i]:
                 t.record_stream(comm_stream)
             return
-        if fp8_transport:
+        if from_wire:
+            wires[i] = fp8.fp8_exchange_wire(chunks[i], D, sp_group,
+                                             rotary_emb=rotary_emb if fuse_rope else None)
+        elif fp8_transport:
             fp8.fp8_all_to_all_many(gather[i], chunks[i], D, sp_group,
                                     rotary_emb=rotary_emb if fuse_rope else None)
         else:
@@ -179,37 +191,50 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             finish_fp8_exchange(pending_gathers.pop(step))
         else:
             acc.current_stream().wait_event(gathered[step])
-        if direct_gather:
-            qv, kv, vv = gather[step]
-        else:
-            qv, kv, vv = (x.flatten(0, 1).permute(1, 2, 0, 3) for x in gather[step])
-            if pad > 0:
-                qv, kv, vv = (x.narrow(2, 0, x.shape[2] - pad) for x in (qv, kv, vv))
-        if rope_fn is not None and rotary_emb is not None and not fuse_rope:
-            qv, kv = rope_fn(qv, kv, *rotary_emb)
         cs = sizes[step]
-        if fused_return_pack:
-            # The return encode reads the [B, cs, S, D] output as it is.
-            results[step] = attention_fn(qv, kv, vv, head_offset=offsets[step],
-                                         attn_mask=attention_mask).type_as(query)
-        elif getattr(attention_fn, "writes_into", False):
-            # The kernel epilogue stores straight into the return-A2A send
-            # layout (W_S, S, B, cs, D): no reshape/pad copies.
+        if from_wire:
+            wire, peers, peer_padding = wires[step]
+            wires[step] = None
             send = torch.empty((W_S, Sq, B, cs, D), device=query.device, dtype=query.dtype)
             if pad > 0:
                 send[-1, Sq - pad:].zero_()
             view = send.flatten(0, 1).permute(1, 2, 0, 3)
-            attention_fn(qv, kv, vv, head_offset=offsets[step], attn_mask=attention_mask,
-                         out=view.narrow(2, 0, W_S * Sq - pad))
+            attention_fn.attend_fp8_wire(wire, peers=peers, seq=Sq, batch=B, heads=cs,
+                                         valid_seq=W_S * Sq - pad, peer_padding=peer_padding,
+                                         out=view.narrow(2, 0, W_S * Sq - pad))
+            wire.record_stream(acc.current_stream())  # allocated on the comm stream
             results[step] = send.flatten(-2, -1)
         else:
-            out = attention_fn(qv, kv, vv, head_offset=offsets[step], attn_mask=attention_mask)
-            out = out.type_as(query)
-            if pad > 0:
-                shape = list(out.shape)
-                shape[2] = pad
-                out = torch.cat([out, out.new_zeros(shape)], dim=2)
-            results[step] = out.unflatten(2, (W_S, -1)).permute(2, 3, 0, 1, 4).flatten(-2, -1)
+            if direct_gather:
+                qv, kv, vv = gather[step]
+            else:
+                qv, kv, vv = (x.flatten(0, 1).permute(1, 2, 0, 3) for x in gather[step])
+                if pad > 0:
+                    qv, kv, vv = (x.narrow(2, 0, x.shape[2] - pad) for x in (qv, kv, vv))
+            if rope_fn is not None and rotary_emb is not None and not fuse_rope:
+                qv, kv = rope_fn(qv, kv, *rotary_emb)
+            if fused_return_pack:
+                # The return encode reads the [B, cs, S, D] output as it is.
+                results[step] = attention_fn(qv, kv, vv, head_offset=offsets[step],
+                                             attn_mask=attention_mask).type_as(query)
+            elif getattr(attention_fn, "writes_into", False):
+                # The kernel epilogue stores straight into the return-A2A send
+                # layout (W_S, S, B, cs, D): no reshape/pad copies.
+                send = torch.empty((W_S, Sq, B, cs, D), device=query.device, dtype=query.dtype)
+                if pad > 0:
+                    send[-1, Sq - pad:].zero_()
+                view = send.flatten(0, 1).permute(1, 2, 0, 3)
+                attention_fn(qv, kv, vv, head_offset=offsets[step], attn_mask=attention_mask,
+                             out=view.narrow(2, 0, W_S * Sq - pad))
+                results[step] = send.flatten(-2, -1)
+            else:
+                out = attention_fn(qv, kv, vv, head_offset=offsets[step], attn_mask=attention_mask)
+                out = out.type_as(query)
+                if pad > 0:
+                    shape = list(out.shape)
+                    shape[2] = pad
+                    out = torch.cat([out, out.new_zeros(shape)], dim=2)
+                results[step] = out.unflatten(2, (W_S, -1)).permute(2, 3, 0, 1, 4).flatten(-2, -1)
         attended[step].record()
         with acc.stream(comm_stream):
             if not gather_priority and pos + 1 < phaa_split_num:
