@@ -57,6 +57,15 @@ def test_argument_errors_without_gpu():
     strides = _lib.i64_array([0, 0, 0, 1])
     assert h.xgb_attention_sage(dummy, dummy, dummy, dummy, dummy, dummy, 1, 1, 0, dummy, strides,
                                 None, 0, None, None) == -2
+    # Sage preparation from the FP8 wire: pointers, layout and alignment
+    prep = lambda *a: h.xgb_sage_prepare_wire(*a)  # noqa: E731
+    ok = (dummy, 2, 64, 1, 3, 100, 0, ctypes.c_float(0.088), dummy, dummy, dummy, dummy, dummy, dummy,
+          dummy, 1 << 20, None)
+    assert prep(None, *ok[1:]) == -1                                   # null payload
+    assert prep(*ok[:5], 129, *ok[6:]) == -2                           # valid_seq > peers * seq
+    assert prep(*ok[:6], 2, *ok[7:]) == -1                             # padding not a multiple of 4
+    assert prep(ctypes.c_void_p(18), *ok[1:]) == -4                    # payload not 4-byte aligned
+    assert prep(*ok[:14], dummy, 16, None) == -7                       # workspace too small
 
 
 def test_ops_refuse_cpu_tensors():
