@@ -35,7 +35,9 @@ ROOT = Path(__file__).resolve().parent
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
-METRIC = "SP attention TFLOP/s/GPU and DiT block ms at 768P-5s, 1/2/4/8 B200"
+# BASELINE.json's metric; `value` is the aggregate over all GPUs (the
+# per-GPU figure is `per_gpu_tflops`), as the metric string says.
+METRIC = "SP attention TFLOP/s (aggregate over GPUs; per GPU in per_gpu_tflops) and DiT block ms at 768P-5s, 1/2/4/8 B200"
 GRID = (31, 48, 84)
 TEXT, AUDIO = 512, 1250
 HEADS, HEAD_DIM = 24, 128
@@ -71,10 +73,12 @@ def parse():
     ap.add_argument("--sp", type=int, default=8, help="SP degree that sets the linear-stack M")
     ap.add_argument("--hbm-kernels", action="store_true",
                     help="time the HBM-bound kernels at one SP rank's shapes (--sp) against the measured HBM copy bandwidth")
+    ap.add_argument("--c5", choices=("auto", "on", "off"), default="auto",
+                    help="BASELINE config 5 (two blocks at 768P-15s, 20 steps): auto = at 8 GPUs only")
     return ap.parse_args()
 
 
-def linear_stack(args, dev=None, quiet=False):
+def linear_stack(args, dev=None, quiet=False, sp=None):
     """the block's FP8 Linear stack (QKV hid->3*hid, O,
     FFN up hid->F, down F->hid) at M = ceil(126,754 / sp) tokens, per-token
     e4m3 activations and per-channel e4m3 weights; times each projection
@@ -85,7 +89,7 @@ def linear_stack(args, dev=None, quiet=False):
 
     dev = dev or torch.device("cuda", 0)
     hid, ffn = 3072, 12288
-    m = -(-SEQ // max(1, args.sp))
+    m = -(-SEQ // max(1, sp if sp is not None else args.sp))
     g = torch.Generator(device=dev).manual_seed(3)
     shapes = {"to_qkv": (3 * hid, hid), "to_out": (hid, hid), "ff_up": (ffn, hid), "ff_down": (hid, ffn)}
     res, total_flops, total_ms = {}, 0.0, 0.0
@@ -262,6 +266,195 @@ def hbm_kernels(args):
                       "l2": "512 MB write between launches"}), flush=True)
 
 
+# ------------------------------------------------------------------ global inputs
+INPUT_BLOCK = 1024  # rows per seeded generator block of the global Q/K/V
+WIDTH = HEADS * HEAD_DIM
+
+
+def global_rows(which: str, start: int, stop: int, dev):
+    """Rows [start, stop) of the global synthetic Q, K or V ([S_pad, 3072]
+    bf16: N(0, 1), K plus a per-head channel bias of
+    variance 4). Each 1024-row block has its own seeded generator, so a span
+    has the same values whatever the SP degree that cuts it: one SP rank's
+    shard and rank 0's copy of the whole sequence agree. Rows at or past the
+    real sequence are the zero padding split_sequence appends."""
+    import torch
+
+    salt = {"q": 1, "k": 2, "v": 3}[which]
+    out = torch.zeros(stop - start, WIDTH, device=dev)
+    for blk in range(start // INPUT_BLOCK, -(-stop // INPUT_BLOCK)):
+        lo, hi = max(start, blk * INPUT_BLOCK), min(stop, (blk + 1) * INPUT_BLOCK, SEQ)
+        if lo >= hi:
+            continue
+        g = torch.Generator(device=dev).manual_seed(salt * 1_000_003 + blk)
+        vals = torch.randn(INPUT_BLOCK, WIDTH, device=dev, generator=g)
+        out[lo - start:hi - start] = vals[lo - blk * INPUT_BLOCK:hi - blk * INPUT_BLOCK]
+    if which == "k":
+        bias = 2.0 * torch.randn(WIDTH, device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+        real = max(0, min(stop, SEQ) - start)
+        out[:real] += bias
+    return out.bfloat16()
+
+
+# ------------------------------------------------------------------ SP parity
+PARITY_ROWS = 64
+
+
+def parity_rows():
+    """The global query rows checked after the timed run: 64 evenly spaced
+    rows of the real sequence, as the reference's block harness samples
+    (tools/benchmark_h3_parallel_block.py:175-189)."""
+    import torch
+
+    return torch.linspace(0, SEQ - 1, PARITY_ROWS, dtype=torch.float64).round().long()
+
+
+def gather_parity_rows(out, rank, world, s_loc, dev):
+    """Every rank contributes the sampled rows of its shard of the layer
+    output [1, S_loc, 3072]; one SUM all-reduce gives every rank all 64."""
+    import torch
+    import torch.distributed as dist
+
+    rows = parity_rows()
+    sel = torch.zeros(PARITY_ROWS, WIDTH, dtype=torch.float32, device=dev)
+    mine = (rows // s_loc) == rank
+    if bool(mine.any()):
+        sel[mine.to(dev)] = out[0, (rows[mine] - rank * s_loc).to(dev)].float()
+    if world > 1:
+        dist.all_reduce(sel)
+    return sel
+
+
+def _bf16(x):
+    return x.bfloat16().float()
+
+
+def _rope_ref(x, cos, sin):
+    """Rotate-half RoPE with bf16 rounding after each operation
+    (x_base/x_base/operator/h3_partial_rope.py:9-29) on [S, 128] fp32 rows
+    holding bf16 values; cos/sin [S, R] fp32."""
+    import torch
+
+    r = cos.shape[-1]
+    half = r // 2
+    c, s = _bf16(cos), _bf16(sin)
+    rot = x[:, :r]
+    partner = torch.cat([-rot[:, half:], rot[:, :half]], dim=1)
+    out = x.clone()
+    out[:, :r] = _bf16(_bf16(rot * c) + _bf16(partner * s))
+    return out
+
+
+def _wire_round_trip(x):
+    """PHAA FP8 wire round trip of rows [N, 128] (x_base/x_base/phaa/
+    fp8_transport.py:26-78): scale = max(max|x| / 448, 1e-12) and
+    e4m3(clamp(x / scale, +-448)) with IEEE divisions, decoded as
+    bf16(e4m3 * scale)."""
+    import torch
+
+    amax = x.abs().amax(dim=1)
+    scale = torch.clamp(amax / torch.full_like(amax, 448.0), min=1e-12)
+    codes = (x / scale[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return _bf16(codes.float() * scale[:, None])
+
+
+def _block_int8(x, rows_per_block=64):
+    """Per-64-row INT8 codes and scales (amax / 127, IEEE; an all-zero block
+    gets scale 1), round-half-even, clamped to +-127."""
+    import torch
+
+    n, d = x.shape
+    nb = -(-n // rows_per_block)
+    xp = torch.zeros(nb * rows_per_block, d, dtype=x.dtype, device=x.device)
+    xp[:n] = x
+    xb = xp.view(nb, rows_per_block, d)
+    amax = xb.abs().amax(dim=(1, 2))
+    scale = torch.where(amax > 0, amax / torch.full_like(amax, 127.0), torch.ones_like(amax))
+    codes = torch.round(xb / scale[:, None, None]).clamp(-127, 127)
+    return codes.view(-1, d)[:n], scale
+
+
+def reference_rows(precision, wire, dev, cos_full, sin_full):
+    """The reference's quantised path for the sampled rows, per head, in
+    plain torch on this GPU (fp64 where the order of a sum matters):
+    RoPE -> [FP8 wire round trip of Q/K/V] -> attention -> bf16 output ->
+    [FP8 wire round trip of the output]. Sage follows the SageAttention2
+    scheme BASELINE config 3 names (the third-party kernel the reference
+    calls, x_base/x_base/operator/attention.py:363-364): K mean-smoothing,
+    per-64-token INT8 Q (sm_scale * log2 e folded in) and K, per-channel
+    e4m3 V, P = exp2(S - rowmax) quantised to e4m3 after a x448 scale, fp32
+    sums. wire: None (SP = 1 or BF16 Ulysses), "fp8" (both directions over
+    the FP8 wire) or "int8" (Sage codes per 16 tokens sent as they are, the
+    output returned over the FP8 wire). Returns (reference [64, 3072], exact
+    fp64 attention of the same RoPE'd bf16 inputs [64, 3072])."""
+    import torch
+
+    qk_block = 16 if wire == "int8" else 64
+    rows = parity_rows().to(dev)
+    q, k, v = (global_rows(w, 0, SEQ, dev) for w in ("q", "k", "v"))
+    cos, sin = cos_full[:SEQ].to(dev), sin_full[:SEQ].to(dev)
+    ref = torch.empty(PARITY_ROWS, WIDTH, device=dev)
+    exact = torch.empty_like(ref)
+    sm_scale = torch.tensor(1.0 / math.sqrt(HEAD_DIM), dtype=torch.float32)
+    qk_scale = float(sm_scale * torch.tensor(1.4426950408889634, dtype=torch.float32))
+    flt_min = torch.finfo(torch.float32).tiny
+    for h in range(HEADS):
+        cols = slice(h * HEAD_DIM, (h + 1) * HEAD_DIM)
+        qh = _rope_ref(q[:, cols].float(), cos, sin)
+        kh = _rope_ref(k[:, cols].float(), cos, sin)
+        vh = v[:, cols].float()
+        p = torch.softmax(qh[rows].double() @ kh.double().T * (1.0 / math.sqrt(HEAD_DIM)), dim=-1)
+        exact[:, cols] = (p @ vh.double()).float()
+        del p
+        if wire == "fp8":
+            qh, kh, vh = (_wire_round_trip(t) for t in (qh, kh, vh))
+        if precision == "sage":
+            q8, sq = _block_int8(qh * qk_scale, qk_block)
+            kmean = kh.double().mean(dim=0).float()
+            k8, sk = _block_int8(kh - kmean, qk_block)
+            vmax = vh.abs().amax(dim=0)
+            sv = torch.clamp(vmax / torch.full_like(vmax, 448.0), min=flt_min)
+            v8 = (vh / sv).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).float()
+            kb = torch.arange(SEQ, device=dev) // qk_block
+            s = (q8[rows].double() @ k8.double().T).float()
+            s = s * sq[rows // qk_block][:, None] * sk[kb][None, :]
+            pr = torch.exp2(s - s.amax(dim=1, keepdim=True))
+            l = pr.double().sum(dim=1).float()
+            p8 = (pr * 448.0).to(torch.float8_e4m3fn).float()
+            o = (p8.double() @ v8.double()).float() * sv[None, :] / (448.0 * l[:, None])
+            del s, pr, p8
+        else:
+            p = torch.softmax(qh[rows].double() @ kh.double().T * (1.0 / math.sqrt(HEAD_DIM)), dim=-1)
+            o = (p @ vh.double()).float()
+            del p
+        o = _bf16(o)
+        ref[:, cols] = _wire_round_trip(o) if wire in ("fp8", "int8") else o
+    return ref, exact
+
+
+def parity_summary(got, ref, exact, precision, wire, world):
+    """Cosine (min over the 24 heads) and max-abs of the gathered rows
+    against the reference path and against exact attention."""
+    def per_head_cos(a, b):
+        a = a.double().view(PARITY_ROWS, HEADS, HEAD_DIM).transpose(0, 1).reshape(HEADS, -1)
+        b = b.double().view(PARITY_ROWS, HEADS, HEAD_DIM).transpose(0, 1).reshape(HEADS, -1)
+        return (a * b).sum(1) / (a.norm(dim=1) * b.norm(dim=1)).clamp_min(1e-300)
+
+    cos_ref = per_head_cos(got, ref)
+    cos_exact = per_head_cos(got, exact)
+    bar = 0.999 if precision == "sage" else 0.9999
+    return {"rows": PARITY_ROWS, "heads": HEADS, "sp": world,
+            "reference": (f"{'Sage INT8/e4m3' if precision == 'sage' else 'fp64 SDPA'} restatement"
+                          + {"fp8": " over the FP8-wire round trip (gather and return)",
+                             "int8": " with INT8 Q/K per 16 tokens on the wire and the FP8-wire return"}.get(wire, "")
+                          + " of the same global seeded inputs"),
+            "cosine_min": float(cos_ref.min()), "cosine_mean": float(cos_ref.mean()),
+            "max_abs": float((got - ref).abs().max()),
+            "cosine_min_vs_exact": float(cos_exact.min()),
+            "max_abs_vs_exact": float((got - exact).abs().max()),
+            "bar": bar, "ok": bool(cos_ref.min() >= bar)}
+
+
 # ------------------------------------------------------------------ helpers
 def dist_env():
     rank = int(os.environ.get("RANK", 0))
@@ -395,6 +588,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": FLOPS_PER_LAYER / (value * 1e12) * 1e3,
+        "ms_per_step_basis": "extrapolated: one 24-head layer at the rate the 1-head sample measured",
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": workload_config(world, "reference-cpu"),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": used, "kind": "port",
@@ -449,8 +643,10 @@ def main():
         group = ParallelManager(1, 1, world, 1).sp_group
     _lib.lib()
 
-    # Workload: pad the packed sequence to a multiple of 16*SP.
-    s_pad = -(-SEQ // (16 * world)) * (16 * world)
+    # Workload: under SP the packed sequence is padded to a multiple of 16*SP
+    # (BASELINE config 2); a single GPU runs it unpadded, as the reference
+    # does without SP.
+    s_pad = SEQ if world == 1 else -(-SEQ // (16 * world)) * (16 * world)
     s_loc = s_pad // world
     get_pad_manager()._pads["mmh3_seq"] = s_pad - SEQ
     cos_full, sin_full = rope_3d(GRID, TEXT + AUDIO)
@@ -459,15 +655,9 @@ def main():
     sin_full = torch.cat([sin_full, pad_rows])
     cos = cos_full[rank * s_loc:(rank + 1) * s_loc].contiguous().to(dev)
     sin = sin_full[rank * s_loc:(rank + 1) * s_loc].contiguous().to(dev)
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    width = HEADS * HEAD_DIM
-    q = torch.randn(1, s_loc, width, device=dev, generator=g).bfloat16()
-    k_bias = torch.randn(1, 1, width, device=dev, generator=torch.Generator(device=dev).manual_seed(7)) * 2.0
-    k = (torch.randn(1, s_loc, width, device=dev, generator=g) + k_bias).bfloat16()
-    v = torch.randn(1, s_loc, width, device=dev, generator=g).bfloat16()
-    if world > 1 and rank == world - 1 and s_pad > SEQ:
-        for t in (q, k, v):  # the tail padding rows are zeros, as split_sequence makes them
-            t[:, s_loc - (s_pad - SEQ):].zero_()
+    # This rank's span of the global inputs (identical global tensors at every
+    # SP degree; the tail padding rows are zeros, as split_sequence makes them).
+    q, k, v = (global_rows(w, rank * s_loc, (rank + 1) * s_loc, dev)[None] for w in ("q", "k", "v"))
 
     backend = H3AttentionBackendB200(args.precision)
     comm_stream = torch.cuda.Stream(device=dev) if world > 1 else None
@@ -511,6 +701,8 @@ def main():
     attn_calls = (backend.kernel_calls - launches_before) // args.steps
     assert kernel_errors(dev) == 0, "a tcgen05 kernel reported a timed-out wait"
     value = FLOPS_PER_LAYER / (ms * 1e-3) / 1e12  # aggregate over all ranks
+    # the timed layer's output at the sampled global rows (checked at the end)
+    parity_got = gather_parity_rows(out, rank, world, s_loc, dev)
 
     # ---- dominant kernel alone: the attention kernel on prepared inputs
     roof = attention_roofline(args.precision, world, dev, s_pad)
@@ -531,6 +723,30 @@ def main():
     if not args.no_block:
         block = block_timing(args, world, rank, dev, group, s_loc, cos, sin, comm_stream, barrier,
                              max_over_ranks)
+        # the block's FP8 Linear stack at this SP degree's M
+        stack = linear_stack(args, dev, quiet=True, sp=world)
+        stack_ms = max_over_ranks(stack["total_ms"])
+        peak_fp8 = roof["peak"] if args.precision == "sage" else gemm_peak(dev, "sage")[0]
+        block["linear_stack_c4"] = {
+            "m": stack["m"], "ms": stack_ms, "tflops_per_gpu": stack["tflops"] * stack["total_ms"] / stack_ms,
+            "frac_of_fp8_peak": stack["tflops"] * stack["total_ms"] / stack_ms / peak_fp8,
+            "per_projection": stack["linear_stack"],
+            "config": "hid 3072, FFN 12288 (GELU: up hid->F), per-token e4m3 activations, per-channel weights"}
+
+    c5 = None
+    if args.c5 == "on" or (args.c5 == "auto" and world == 8):
+        c5 = c5_timing(args, world, rank, dev, group, comm_stream, barrier, max_over_ranks)
+
+    # ---- SP parity of the timed layer (outside every timed region): rank 0
+    # recomputes the sampled rows through the reference's quantised path
+    parity = None
+    if rank == 0:
+        wire = None if world == 1 or args.precision != "sage" else args.wire
+        ref, exact = reference_rows(args.precision, wire, dev, cos_full, sin_full)
+        parity = parity_summary(parity_got, ref, exact, args.precision, wire, world)
+        del ref, exact
+        torch.cuda.empty_cache()
+    barrier()
 
     kernels_per_layer = kernels_per_step(args.precision, world, min(args.phaa_num, HEADS // world),
                                          args.wire)
@@ -543,7 +759,7 @@ def main():
         "per_gpu_tflops": value / world, "attention_calls_per_step": attn_calls,
         "gpu_launches": kernels_per_layer * args.steps,
         "clocks": clocks.summary(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-        "block": block,
+        "block": block, "c5": c5, "parity": parity,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -602,6 +818,81 @@ def block_timing(args, world, rank, dev, group, s_loc, cos, sin, comm_stream, ba
             "config": "hidden 3072, 24x128 heads, FFN 12288 GELU, AdaLN LayerNorm, FP8 per-token linears"}
 
 
+GRID_15S = (93, 48, 84)
+AUDIO_15S = 3750
+SEQ_15S = GRID_15S[0] * GRID_15S[1] * GRID_15S[2] + TEXT + AUDIO_15S  # 379,238
+
+
+def c5_timing(args, world, rank, dev, group, comm_stream, barrier, max_over_ranks):
+    """two stacked H3 DiT blocks (hidden 3072, 24 x 128
+    heads, FFN 12288 GELU, Sage-FP8 attention, FP8 per-token linears,
+    random-init weights) at the 768P-15s shape (93x48x84 video + 512 text +
+    3,750 audio = 379,238 tokens), SP = the job's GPUs over NCCL, timed over
+    20 denoising-step invocations, each with its own random AdaLN rows (the
+    step's cached table). Reports ms per block and TFLOP/s per GPU (the
+    reference harness's units, tools/benchmark_h3_parallel_block.py:153-170)."""
+    import torch
+
+    from xgen_b200.h3.block import H3BlockConfig, H3DiTBlockB200
+    from xgen_b200.h3.rope import rope_3d
+
+    torch.cuda.empty_cache()
+    steps, n_blocks = 20, 2
+    s_pad = SEQ_15S if world == 1 else -(-SEQ_15S // (16 * world)) * (16 * world)
+    s_loc = s_pad // world
+    from xgen_b200.sp.padding import get_pad_manager
+
+    get_pad_manager()._pads["mmh3_seq"] = s_pad - SEQ_15S
+    cos, sin = rope_3d(GRID_15S, TEXT + AUDIO_15S)
+    cos = torch.cat([cos, torch.ones(s_pad - SEQ_15S, HEAD_DIM)])[rank * s_loc:(rank + 1) * s_loc]
+    sin = torch.cat([sin, torch.zeros(s_pad - SEQ_15S, HEAD_DIM)])[rank * s_loc:(rank + 1) * s_loc]
+    cos, sin = cos.contiguous().to(dev), sin.contiguous().to(dev)
+    cfg = H3BlockConfig(hidden=3072, heads=HEADS, head_dim=HEAD_DIM, ffn=12288, activation="gelu",
+                        norm="layernorm", precision=args.precision)
+    blocks = [H3DiTBlockB200(H3DiTBlockB200.random_weights(cfg, seed=100 + i), cfg, dev)
+              for i in range(n_blocks)]
+    g = torch.Generator(device=dev).manual_seed(500 + rank)
+    x = torch.randn(1, s_loc, cfg.hidden, device=dev, generator=g).bfloat16()
+    if rank == world - 1 and s_pad > SEQ_15S:
+        x[:, s_loc - (s_pad - SEQ_15S):].zero_()
+    tg = torch.Generator(device=dev).manual_seed(55)  # the same tables on every rank
+    tables = [(0.1 * torch.randn(3, 6 * cfg.hidden, device=dev, generator=tg)).bfloat16()
+              for _ in range(steps)]
+    tags = torch.zeros(s_pad, dtype=torch.int64)
+    video = GRID_15S[0] * GRID_15S[1] * GRID_15S[2]
+    tags[video:video + TEXT] = 1
+    tags[video + TEXT:SEQ_15S] = 2
+    idx = tags[rank * s_loc:(rank + 1) * s_loc].to(dev)
+
+    def invocation(table):
+        h = x
+        for blk in blocks:
+            h = blk.forward(h, table, idx, (cos, sin), sp_group=group, sp_size=world,
+                            phaa_num=min(args.phaa_num, HEADS // world),
+                            fp8_transport=args.precision == "sage", comm_stream=comm_stream)
+        return h
+
+    for i in range(3):
+        invocation(tables[i])
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for table in tables:
+        out = invocation(table)
+    e.record()
+    barrier()
+    ms = max_over_ranks(s.elapsed_time(e)) / (steps * n_blocks)
+    attention = 4.0 * SEQ_15S * SEQ_15S * HEAD_DIM * HEADS / world  # per GPU per block
+    gemm = blocks[0].flops(s_loc, SEQ_15S)
+    del out, blocks, x
+    torch.cuda.empty_cache()
+    return {"workload": "h3-2-blocks-768p15s", "seq_real": SEQ_15S, "grid": list(GRID_15S),
+            "sp": world, "blocks": n_blocks, "steps": steps, "ms_per_block": ms,
+            "ms_per_step": ms * n_blocks, "tflops_per_gpu": (attention + gemm) / ms / 1e9,
+            "attention_flops_per_gpu_block": attention, "gemm_flops_per_gpu_block": gemm,
+            "adaln": "a fresh random [3, 6*3072] table per step"}
+
+
 def kernels_per_step(precision, world, phaa, wire="fp8"):
     """Our kernel launches per layer: SP=1: RoPE + (Sage: 3 prepare + 1 attention).
     SP>1 per PHAA chunk: QKV encode, decode, (Sage: 3 prepare) + attention,
@@ -627,7 +918,9 @@ def attention_roofline(precision, world, dev, s_pad):
     heads = HEADS // world
     g = torch.Generator(device=dev).manual_seed(99)
     q = torch.randn(1, heads, SEQ, HEAD_DIM, device=dev, generator=g).bfloat16()
-    k = torch.randn(1, heads, SEQ, HEAD_DIM, device=dev, generator=g).bfloat16()
+    # K with the workload's per-head channel bias (variance 4)
+    k = (torch.randn(1, heads, SEQ, HEAD_DIM, device=dev, generator=g)
+         + 2.0 * torch.randn(1, heads, 1, HEAD_DIM, device=dev, generator=g)).bfloat16()
     v = torch.randn(1, heads, SEQ, HEAD_DIM, device=dev, generator=g).bfloat16()
     out = torch.empty_like(q)
     if precision == "sage":

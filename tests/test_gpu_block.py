@@ -134,3 +134,45 @@ def test_norm_modulate_quant_widths(cuda_device, norm, h):
     assert ((mod.float() - ref_mod.float()).abs() <= bound).all()
     rc, rs = quantize_per_token(mod.reshape(b * s, h))
     assert torch.equal(scales, rs) and torch.equal(codes.view(torch.uint8), rc.view(torch.uint8))
+
+
+@pytest.mark.parametrize("precision", ["sage", "bf16"])
+def test_config1_block_at_stated_shape(cuda_device, precision):
+    """BASELINE config 1 at its stated shape: 4,096 video tokens of a
+    4x32x32 latent grid + 256 text tokens, hidden 1536, 12 x 128 heads, 3-D
+    RoPE (theta 10000, head dims 32/48/48 over t/h/w), AdaLN LayerNorm from
+    one random 6 x 1536 row, GELU FFN 6144, activations N(0, 1), weights
+    N(0, 0.02), seed 0; the B200 block (FP8 per-token projections, Sage or
+    BF16 attention) against the unquantised fp32 restatement of the
+    reference block (h3_npu_fusion.py:339-356).
+
+    Tolerance on the branch output d = y - x (FP8 error compounds over the
+    four projections; the reference's own FP8-vs-BF16 gate is rel-RMSE < 0.08
+    per projection): cosine >= 0.995, rel-RMSE <= 0.08, and max |y - ref|
+    <= 0.15 (|y| reaches ~5)."""
+    from xgen_b200.h3.block import H3BlockConfig, H3DiTBlockB200
+    from xgen_b200.h3.rope import rope_3d
+
+    cfg = H3BlockConfig(hidden=1536, heads=12, head_dim=128, ffn=6144, activation="gelu",
+                        norm="layernorm", precision=precision)
+    cos, sin = rope_3d((4, 32, 32), 256, split=(32, 48, 48), theta=10000.0)
+    s = cos.shape[0]
+    assert s == 4352
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, s, cfg.hidden, generator=g).bfloat16()
+    table = torch.randn(1, 6 * cfg.hidden, generator=g).bfloat16()
+    idx = torch.zeros(s, dtype=torch.int64)
+    w = H3DiTBlockB200.random_weights(cfg, seed=0)
+    blk = H3DiTBlockB200(w, cfg, cuda_device)
+    dev = cuda_device
+    y = blk.forward(x.to(dev), table.to(dev), idx.to(dev), (cos.to(dev), sin.to(dev)))
+    torch.cuda.synchronize()
+    ref = ob.block_forward(x.float(), w, table, idx, cos, sin, cfg)
+    got = y.float().cpu()
+    assert torch.isfinite(got).all()
+    d_got, d_ref = got - x.float(), ref - x.float()
+    cos_sim = cosine(d_got.numpy(), d_ref.numpy())
+    rel_rmse = float((d_got - d_ref).pow(2).mean().sqrt() / d_ref.pow(2).mean().sqrt())
+    max_abs = float((got - ref).abs().max())
+    print(f"config1 {precision}: cosine {cos_sim:.6f} rel-RMSE {rel_rmse:.4f} max-abs {max_abs:.4f}")
+    assert cos_sim >= 0.995 and rel_rmse <= 0.08 and max_abs <= 0.15, (cos_sim, rel_rmse, max_abs)

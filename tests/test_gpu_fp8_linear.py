@@ -89,6 +89,29 @@ def test_per_token_gemm_matches_oracle(cuda_device):
     assert_gemm_close(got, ref)
 
 
+@pytest.mark.parametrize("offset", [1, 4])
+def test_per_token_quantize_misaligned_output(cuda_device, offset):
+    """A C-ABI caller may hand xgb_fp8_quantize_per_token an output that is
+    not 8-byte aligned: it must take the byte-store path and give the same
+    codes and scales as the aligned call and the oracle."""
+    from xgen_b200 import _lib
+    from xgen_b200.ops import quantize_per_token
+
+    g = torch.Generator().manual_seed(5)
+    rows, cols = 37, 3072
+    x = (torch.randn(rows, cols, generator=g) * 3).bfloat16().to(cuda_device)
+    codes, scales = quantize_per_token(x)
+    buf = torch.zeros(rows * cols + 16, dtype=torch.uint8, device=cuda_device)
+    sc = torch.empty(rows, dtype=torch.float32, device=cuda_device)
+    _lib.call("xgb_fp8_quantize_per_token", x.data_ptr(), _lib.XGB_BF16, rows, cols, x.stride(0),
+              buf.data_ptr() + offset, sc.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    got = buf[offset:offset + rows * cols].view(rows, cols)
+    assert torch.equal(got, codes.view(torch.uint8)) and torch.equal(sc, scales)
+    qa, sa = of.quantize_per_token(x.float().cpu().numpy())
+    assert np.array_equal(got.cpu().numpy(), qa) and np.array_equal(sc.cpu().numpy(), sa)
+    assert int(buf[:offset].sum()) == 0 and int(buf[offset + rows * cols:].sum()) == 0
+
+
 def test_gated_epilogue_matches_gemm_then_indexed_affine(cuda_device):
     """attn_out -> x + gate[idx] * attn_out with the reference's rounding,
     fused vs GEMM followed by the (bit-exact) indexed-affine kernel."""

@@ -217,3 +217,37 @@ def test_sage_from_wire_matches_decode_path(cuda_device, fuse_rope):
     finally:
         get_pad_manager().clear()
     assert torch.equal(wire, decoded)
+
+
+def test_sage_fp16_activations_take_the_decode_path(cuda_device):
+    """fp16 activations with the FP8 wire and a Sage backend: the wire
+    decode rounds to fp16 (the reference's _decode writes the destination
+    dtype), so PHAA must not hand the wire to the bf16-only wire preparation;
+    it decodes into fp16 gather buffers and calls the backend on them."""
+    from xgen_b200.attention import H3AttentionBackendB200
+    from xgen_b200.phaa import phaa_attention
+
+    backend = H3AttentionBackendB200("sage")
+
+    class ViaDecode:
+        writes_into = True
+
+        def __call__(self, q, k, v, **kw):
+            return backend(q, k, v, **kw)
+
+    g = torch.Generator(device=cuda_device).manual_seed(23)
+    qkv = [torch.randn((1, 256, 4 * 128), device=cuda_device, generator=g).half() for _ in range(3)]
+    options = dict(comm_stream=torch.cuda.Stream(), sp_group=None, sp_size=2, heads=4,
+                   phaa_split_num=1, head_dim=128, fp8_transport=True)
+
+    def refuse(*args, **kwargs):
+        raise AssertionError("the wire preparation must not see fp16 activations")
+
+    with patch.object(dist, "get_world_size", return_value=2), \
+         patch.object(dist, "all_to_all_single", side_effect=_local_copy), \
+         patch.object(backend, "attend_fp8_wire", side_effect=refuse):
+        got = phaa_attention.run_phaa_attention(*qkv, attention_fn=backend, **options)
+        expect = phaa_attention.run_phaa_attention(*qkv, attention_fn=ViaDecode(), **options)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float16 and torch.isfinite(got.float()).all()
+    assert torch.equal(got, expect)

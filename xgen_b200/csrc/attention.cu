@@ -57,11 +57,13 @@ constexpr float kNegInf = -__builtin_huge_valf();
 constexpr float kLog2PScale = 4.807354922057604f;
 // One pair of exp2 in kPolyPairs runs as a packed fp32x2 polynomial
 // (ex2_poly2) on the FMA pipe instead of two MUFU ops in the Sage kernel,
-// easing the MUFU load of the exp section a little: measured on B200, 1 in 8
-// pairs gains ~2 % (768P-5s); larger shares lose, because the exp section is bound by
-// issue and latency rather than by MUFU throughput. 0 disables it.
+// easing the MUFU load of the exp section a little. Measured on B200
+// (768P-5s, accumulator init on): 1 in 6 pairs is best (1,526 TFLOP/s at 24
+// heads against 1,490 for 1 in 8, 1,491 for 1 in 4, 1,477 for 1 in 3);
+// larger shares lose, because the exp section is bound by issue and
+// dependency latency rather than by MUFU throughput. 0 disables it.
 #ifndef XGB_ATTN_POLY_PAIRS
-#define XGB_ATTN_POLY_PAIRS 8
+#define XGB_ATTN_POLY_PAIRS 6
 #endif
 constexpr int kPolyPairs = XGB_ATTN_POLY_PAIRS;
 __device__ __forceinline__ bool poly_pair(int pair) {
@@ -71,6 +73,20 @@ __device__ __forceinline__ bool poly_pair(int pair) {
 #define XGB_ATTN_TURN 1
 #endif
 constexpr bool kTurn = XGB_ATTN_TURN != 0;
+// Sage S accumulators start at the bit pattern 0x4B400000 (the float
+// 12582912.0) instead of 0: one kind::f8f6f4 MMA of two constant e5m2 tiles
+// (every A byte 1536, every B byte 256: 32 * 1536 * 256 = 12582912, exact in
+// fp32) writes it before the INT8 QK^T accumulates onto it in s32. The
+// scores then arrive as the exact floats 12582912 + s (|s| < 2^21), with no
+// per-score integer add in the softmax. The constant tiles cost 24 KB of
+// shared memory and 1/16 more tensor work per S tile. 0 disables it (the
+// softmax then adds the pattern itself).
+#ifndef XGB_ATTN_INIT_MMA
+#define XGB_ATTN_INIT_MMA 1
+#endif
+constexpr bool kInitMma = XGB_ATTN_INIT_MMA != 0;
+constexpr uint32_t kInitAWord = 0x66666666u;  // e5m2 1536 in every byte
+constexpr uint32_t kInitBWord = 0x5C5C5C5Cu;  // e5m2 256 in every byte
 constexpr int kTurnBar = 1;  // named barriers 1, 2: exp turn of WG0, WG1
 constexpr int kEpiBar = 3;   // named barrier 3: the 256 softmax threads in the split epilogue
 constexpr uint32_t kMagic = 0x4B400000u;
@@ -88,12 +104,19 @@ struct Cfg {
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQT * kQBytes;
   static constexpr int kVOff = kKOff + kStages * kKVBytes;
-  static constexpr int kBarOff = kVOff + kStages * kKVBytes;
+  // Sage accumulator-init operands (XGB_ATTN_INIT_MMA): 128 and 64 rows of
+  // 128 bytes, SW128 K-major like Q and K (all bytes equal, so the swizzle
+  // does not matter).
+  static constexpr bool kInit = kSage && kInitMma;
+  static constexpr int kInitAOff = kVOff + kStages * kKVBytes;
+  static constexpr int kInitBOff = kInitAOff + (kInit ? kBM * 128 : 0);
+  static constexpr int kBarOff = kInitBOff + (kInit ? kBN * 128 : 0);
   static constexpr int kSmem = kBarOff + 512 + 1024;  // + barriers + alignment slack
   static constexpr uint32_t kIdescQK =
       kSage ? instr_desc(2, 1, 1, false, false, kBM, kBN) : instr_desc(1, 1, 1, false, false, kBM, kBN);
   static constexpr uint32_t kIdescPV =
       kSage ? instr_desc(1, 0, 0, false, true, kBM, kD) : instr_desc(1, 1, 1, false, true, kBM, kD);
+  static constexpr uint32_t kIdescInit = instr_desc(1, 1, 1, false, false, kBM, kBN);  // e5m2 x e5m2 -> f32
 };
 
 struct Params {
@@ -221,6 +244,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_barrier_init();
   }
+  if constexpr (C::kInit) {
+    uint4* init = reinterpret_cast<uint4*>(smem + C::kInitAOff);
+    for (int j = threadIdx.x; j < (kBM + kBN) * 128 / 16; j += kThreads) {
+      const uint32_t w = j < kBM * 128 / 16 ? kInitAWord : kInitBWord;
+      init[j] = make_uint4(w, w, w, w);
+    }
+    fence_proxy_async_smem();  // the tensor core reads them through the async proxy
+  }
   if (warp == kMmaWarp) tmem_alloc<512>(&bars->tmem_base);
   if (warp == kTmaWarp && lane == 0) {
     prefetch_tmap(&q_map);
@@ -270,12 +301,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr Kind kQK = kSage ? Kind::kI8 : Kind::kF16;
       constexpr Kind kPV = kSage ? Kind::kF8F6F4 : Kind::kF16;
       // S_i(t) -> buffer t%2 of Q tile i, publish on s_full[i][t%2].
+      const uint64_t init_a = smem_desc_sw128(smem_u32(smem + C::kInitAOff), 16, 1024);
+      const uint64_t init_b = smem_desc_sw128(smem_u32(smem + C::kInitBOff), 16, 1024);
       auto issue_s = [&](int t) {
         const uint32_t ka = k_saddr + (t % C::kStages) * C::kKVBytes;
+        if constexpr (C::kInit)  // S = 0x4B400000 in every element, then += Q.K^T
+          mma_ss<Kind::kF8F6F4>(tmem + s_col(i, t & 1), init_a, init_b, C::kIdescInit, false);
 #pragma unroll
         for (int k = 0; k < C::kKStepsD; ++k)
           mma_ss<kQK>(tmem + s_col(i, t & 1), kmajor_desc<kSage>(qa, k, kBM * 128),
-                      kmajor_desc<kSage>(ka, k, C::kSub), C::kIdescQK, k > 0);
+                      kmajor_desc<kSage>(ka, k, C::kSub), C::kIdescQK, C::kInit || k > 0);
         tc_commit(&bars->s_full[i][t & 1]);
       };
       bool ok = mbar_wait(&bars->q_full, 0, p.err);
@@ -364,9 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(s_addr, r[0]);
       tmem_ld32(s_addr + 32, r[1]);
       tmem_ld_wait();
-      // Sage: int32 accumulators become exact floats 12582912 + s by adding
-      // 0x4B400000 to their bits (|s| < 2^22: 128 products of |int8| <=
-      // 127), a monotone map, so the max runs on floats and no conversion
+      // Sage: the int32 scores s are read as the exact floats 12582912 + s:
+      // their accumulator started at the bits 0x4B400000 (kInit), or the
+      // pattern is added here (|s| < 2^22: 128 products of |int8| <= 127).
+      // The map is monotone, so the max runs on floats and no conversion
       // instruction is needed. Padding keys (>= valid, last tile only) get a
       // sentinel far below any real score.
       const int valid = p.seq_kv - (kv0 + t) * kBN;
@@ -382,10 +418,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if constexpr (kSage) {
         if (!kWire && t + 1 < n_kv) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0 + t + 1];
+        if constexpr (!C::kInit) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r[c][e] += kMagic;
+            for (int e = 0; e < 32; ++e) r[c][e] += kMagic;
+        }
       }
       if (valid < kBN) {
         const uint32_t sentinel = kSage ? 0x4B000000u /* 12582912 - 2^22 */ : 0xFF800000u /* -inf */;

@@ -117,8 +117,10 @@ __global__ void __launch_bounds__(kThreads) per_token_kernel(const T* __restrict
   if (row >= rows) return;
   const T* src = x + row * row_stride;
   uint8_t* dst = out + row * cols;
+  // 16-byte loads and 8-byte stores need both x and out aligned for them.
   const bool vec = cols % 8 == 0 && row_stride % 8 == 0 &&
-                   (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+                   (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 7u) == 0;
   int m = 0;
   if (vec) {
     for (int64_t c = lane * 8; c < cols; c += 256) {

@@ -27,6 +27,7 @@
 //              AdaLN gate and residual move as 16-byte vectors
 // Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile run
 // under the MMAs of the next. Every mbarrier wait is bounded.
+#include <atomic>
 #include <cstdlib>
 
 #include "sm100.cuh"
@@ -424,6 +425,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tma_load_2d_pair(st + kPairABytes, &b_map, full0, kb * kBK, n0);
         }
       }
+      // After a timed-out wait, rank 0 drains the stages it armed before the
+      // CTAs leave: their full barrier completes only once both CTAs' loads
+      // have landed (bounded, like every wait). On the normal path the MMA
+      // issuer has consumed every stage, so these waits return at once.
+      if (!ok && rank == 0) {
+        for (int i = max(0, it - kPairStages); i < it; ++i)
+          mbar_wait(&bars->full[i % kPairStages], (i / kPairStages) & 1, nullptr, 100000000ull);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (rank 0)
@@ -503,12 +512,19 @@ bool pairs_enabled() {
 // Pairs of this kernel that can be resident at once (0 if the pair launch is
 // unavailable): the persistent grid is sized to it so no pair waits for
 // another to finish.
-template <typename Kernel>
-int pair_slots(Kernel kernel) {
+template <int kEpi>
+int pair_slots() {
+  auto kernel = gemm_fp8_pair_kernel<kEpi>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem) != cudaSuccess)
     return 0;
-  static int cached = -1;  // one per kernel instantiation; every B200 has the same SMs
-  if (cached >= 0) return cached;
+  // Measured once per epilogue instantiation and device (its register and
+  // shared-memory use set the occupancy); stored as clusters + 1, 0 = not yet.
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> cached[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  const int known = cached[dev].load(std::memory_order_relaxed);
+  if (known > 0) return known - 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * static_cast<unsigned>(sm_count()));
   cfg.blockDim = dim3(kThreads);
@@ -518,7 +534,7 @@ int pair_slots(Kernel kernel) {
     cudaGetLastError();
     clusters = 0;
   }
-  cached = clusters;
+  cached[dev].store(clusters + 1, std::memory_order_relaxed);
   return clusters;
 }
 
@@ -540,7 +556,7 @@ int launch(const void* a, const void* w, const Params& p, cudaStream_t st) {
     if (!make_tensor_map(&bm2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, bdims, astr, bbox2))
       return XGB_ERR_ALIGN;
     auto kernel = gemm_fp8_pair_kernel<kEpi>;
-    const int max_pairs = pair_slots(kernel);
+    const int max_pairs = pair_slots<kEpi>();
     if (max_pairs > 0) {
       const int tiles = ((p.M + 2 * kPairRows - 1) / (2 * kPairRows)) * ((p.N + kBN - 1) / kBN);
       const int grid = 2 * std::min(tiles, max_pairs);

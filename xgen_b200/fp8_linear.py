@@ -36,9 +36,13 @@ def quantize_per_tensor(value: torch.Tensor):
 
 
 def quantize_per_channel(value: torch.Tensor):
-    """Per-row (output channel) e4m3 of a [out, in] weight."""
+    """Per-row (output channel) e4m3 of a [out, in] weight. The scale is an
+    IEEE division by a tensor 448 (a Python-scalar divisor becomes a
+    reciprocal multiply on CUDA tensors only), so the codes do not depend on
+    the device the weight is quantised on."""
     maximum = torch.finfo(torch.float8_e4m3fn).max
-    scale = (value.float().abs().amax(dim=1) / maximum).clamp_min(torch.finfo(torch.float32).tiny)
+    amax = value.float().abs().amax(dim=1)
+    scale = (amax / torch.full_like(amax, maximum)).clamp_min(torch.finfo(torch.float32).tiny)
     return (value.float() / scale[:, None]).clamp(-maximum, maximum).to(torch.float8_e4m3fn), scale
 
 
@@ -187,55 +191,63 @@ class H3FP8Linear(nn.Module):
 
 
 class H3FP8TPLinear(H3FP8Linear):
-    """H3FP8Linear inside tensor parallelism, keeping the column/row
-    communication of the layer it replaces (x_base/x_base/operator/h3_fp8.py
-    :71-108): column-parallel layers apply their bias locally and optionally
-    all-gather the output; row-parallel layers take (or slice) their input
-    shard, all-reduce the partial products (or call `reduce_fn`) and add the
-    bias after the reduction. Set `activation_group` to share one activation
-    scale across the group (MAX all-reduce before packing).
+    """H3FP8Linear inside tensor parallelism, keeping the communication of
+    the TP layer it replaces (x_base/x_base/operator/h3_fp8.py:71-108).
 
-    `original` carries weight/bias and the TP attributes `column_parallel`
-    (or is an instance named ColumnParallelLinear), `gather_output`,
-    `input_is_parallel`, `tp_group`, `reduce_fn`. With `tp_group` None the
-    layer uses the group `ParallelManager` registered (xgen_b200.tp_state),
-    and runs unsharded when none is registered, as the reference's TP layers
-    do."""
+    A column-parallel layer holds a slice of the output features: it adds
+    its bias locally and, with `gather_output`, all-gathers the slices along
+    the feature axis. A row-parallel layer holds a slice of the input
+    features: it takes its slice of a full input (when `input_is_parallel`
+    is false), and its partial products are summed over the group (all-reduce,
+    or the layer's `reduce_fn(output, group)`) before the bias is added once.
+
+    The TP attributes are read from the replaced layer: `column_parallel`
+    (else: is it a ColumnParallelLinear), `gather_output`,
+    `input_is_parallel`, `tp_group`, `reduce_fn`. Without a `tp_group` the
+    group registered by ParallelManager (xgen_b200.tp_state) is used, and
+    the layer runs unsharded when none is. Set `activation_group` to share
+    one activation scale over a group (MAX all-reduce before packing)."""
+
+    _TP_ATTRIBUTES = (("gather_output", False), ("input_is_parallel", True), ("tp_group", None),
+                      ("reduce_fn", None))
 
     def __init__(self, original, scaling: str = "per_tensor"):
-        bias = getattr(original, "bias", None)
-        super().__init__(original.weight, bias, scaling=scaling)
-        column = getattr(original, "column_parallel", None)
-        self.column_parallel = (type(original).__name__ == "ColumnParallelLinear"
-                                if column is None else bool(column))
-        self.gather_output = getattr(original, "gather_output", False)
-        self.input_is_parallel = getattr(original, "input_is_parallel", True)
-        self.tp_group = getattr(original, "tp_group", None)
-        self.reduce_fn = getattr(original, "reduce_fn", None)
+        super().__init__(original.weight, getattr(original, "bias", None), scaling=scaling)
+        declared = getattr(original, "column_parallel", None)
+        self.column_parallel = (bool(declared) if declared is not None
+                                else type(original).__name__ == "ColumnParallelLinear")
+        for name, default in self._TP_ATTRIBUTES:
+            setattr(self, name, getattr(original, name, default))
 
-    def forward(self, x):
+    def _gather_columns(self, output, group, world):
         import torch.distributed as dist
 
+        slices = [torch.empty_like(output) for _ in range(world)]
+        dist.all_gather(slices, output, group=group)
+        return torch.cat(slices, dim=-1)
+
+    def _reduce_rows(self, output, group):
+        import torch.distributed as dist
+
+        if self.reduce_fn is not None:
+            return self.reduce_fn(output, group)
+        dist.all_reduce(output, group=group)
+        return output
+
+    def forward(self, x):
         from . import tp_state
 
         group, world, rank = tp_state.resolve(self.tp_group)
-        if not self.column_parallel and not self.input_is_parallel and world > 1:
-            x = x.chunk(world, dim=-1)[rank]
-        bias = self.bias
-        if not self.column_parallel:
-            self.bias = None  # row bias belongs after the reduction
-        try:
+        sharded = world > 1
+        if self.column_parallel:
             output = self._forward(x, None)
+            return self._gather_columns(output, group, world) if sharded and self.gather_output else output
+        if sharded and not self.input_is_parallel:
+            x = x.chunk(world, dim=-1)[rank]
+        bias, self.bias = self.bias, None  # the row bias is added once, after the sum
+        try:
+            partial = self._forward(x, None)
         finally:
             self.bias = bias
-        if world > 1:
-            if self.column_parallel and self.gather_output:
-                values = [torch.empty_like(output) for _ in range(world)]
-                dist.all_gather(values, output, group=group)
-                output = torch.cat(values, dim=-1)
-            elif not self.column_parallel:
-                if self.reduce_fn is None:
-                    dist.all_reduce(output, group=group)
-                else:
-                    output = self.reduce_fn(output, group)
-        return output + bias if not self.column_parallel and bias is not None else output
+        total = self._reduce_rows(partial, group) if sharded else partial
+        return total if bias is None else total + bias

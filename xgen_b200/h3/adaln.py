@@ -14,7 +14,8 @@ modality row indices, and the local sequence span.
   SP rank per block computes linear(silu(temb)) and broadcasts it.
 - `adaln_indices` is minimax_h3.py:410-415: row = t_idx * 3 + modality tag,
   plus the pad mask of negative tags.
-- `LocalSpan` mirrors x_diffusers/.../h3_local_io.py:14-38.
+- `LocalSpan` (defined in h3/local_io.py, re-exported here) is the rank's
+  block of the packed sequence, x_diffusers/.../h3_local_io.py:14-38.
 
 safetensors is not a dependency: `SafetensorsFile` / `write_safetensors`
 implement its published layout (little-endian u64 header length, a JSON
@@ -27,12 +28,12 @@ import json
 import logging
 import os
 import struct
-from dataclasses import dataclass
-
 import numpy as np
 import torch
 import torch.distributed as dist
 from torch import nn
+
+from .local_io import LocalSpan  # noqa: F401  (re-exported)
 
 logger = logging.getLogger(__name__)
 
@@ -272,32 +273,3 @@ class H3OwnedAdaLN(nn.Module):
         src = dist.get_global_rank(self.group, self.owner) if self.group is not None else self.owner
         dist.broadcast(output, src=src, group=self.group)
         return output.reshape(-1, 6 * self.hidden_size).chunk(6, dim=-1)
-
-
-@dataclass(frozen=True)
-class LocalSpan:
-    """Contiguous ownership of ceil(total / peers) rows per rank."""
-
-    start: int
-    length: int
-    valid: int
-
-    @classmethod
-    def for_rank(cls, total: int, peers: int, rank: int) -> "LocalSpan":
-        if total < 1 or peers < 1 or not 0 <= rank < peers:
-            raise ValueError("Invalid H3 local sequence layout")
-        length = (total + peers - 1) // peers
-        start = rank * length
-        return cls(start, length, max(0, min(length, total - start)))
-
-    def slice_padded(self, tensor: torch.Tensor, dim: int = 0, value=0) -> torch.Tensor:
-        local = tensor.narrow(dim, min(self.start, tensor.shape[dim]), self.valid)
-        if self.valid == self.length:
-            return local.contiguous()
-        shape = list(local.shape)
-        shape[dim] = self.length - self.valid
-        return torch.cat((local, tensor.new_full(shape, value)), dim=dim)
-
-    def indices(self, packed_indices: torch.Tensor):
-        source = ((packed_indices >= self.start) & (packed_indices < self.start + self.valid)).nonzero().flatten()
-        return source, packed_indices.index_select(0, source) - self.start

@@ -41,7 +41,7 @@ class H3BlockConfig:
     heads: int = 24
     head_dim: int = 128
     ffn: int = 12288
-    activation: str = "gelu"      # "gelu" or "swiglu" (reference model)
+    activation: str = "gelu"      # "gelu" (erf), "gelu_tanh", or "swiglu" (reference model)
     norm: str = "layernorm"       # "layernorm" (BASELINE) or "rmsnorm" (reference model)
     qk_norm: bool = False         # per-head Q/K RMSNorm (reference model)
     eps: float = 1e-6
@@ -51,31 +51,45 @@ class H3BlockConfig:
 
 class H3DiTBlockB200:
     def __init__(self, weights: dict, config: H3BlockConfig, device):
-        c = self.config = config
-        self.device = device
+        c = config
         lin = lambda name: H3FP8Linear(weights[name], weights.get(name + ".bias"),  # noqa: E731
                                        scaling=c.fp8_scaling).to(device)
-        self.to_qkv = lin("to_qkv")
-        self.to_out = lin("to_out")
-        self.ff_up = lin("ff_up")
+        norm_q = norm_k = None
+        if c.qk_norm:
+            norm_q = torch.nn.RMSNorm(c.head_dim, eps=c.eps).to(device, torch.bfloat16)
+            norm_k = torch.nn.RMSNorm(c.head_dim, eps=c.eps).to(device, torch.bfloat16)
+            norm_q.weight.data.copy_(weights["norm_q.weight"])
+            norm_k.weight.data.copy_(weights["norm_k.weight"])
+        n1, n2 = weights.get("norm1.weight"), weights.get("norm2.weight")
+        self._attach(config, device, lin("to_qkv"), lin("to_out"), lin("ff_up"), lin("ff_down"),
+                     n1.to(device, torch.bfloat16) if n1 is not None else None,
+                     n2.to(device, torch.bfloat16) if n2 is not None else None,
+                     norm_q, norm_k, H3AttentionBackendB200(c.precision))
+
+    @classmethod
+    def from_modules(cls, config: H3BlockConfig, device, *, to_qkv, to_out, ff_up, ff_down,
+                     norm1_weight=None, norm2_weight=None, norm_q=None, norm_k=None,
+                     attention=None) -> "H3DiTBlockB200":
+        """The block over FP8 projections and norms that already exist (those
+        an installed H3 module holds), sharing them rather than copying."""
+        blk = cls.__new__(cls)
+        blk._attach(config, device, to_qkv, to_out, ff_up, ff_down, norm1_weight, norm2_weight,
+                    norm_q, norm_k, attention or H3AttentionBackendB200(config.precision))
+        return blk
+
+    def _attach(self, config, device, to_qkv, to_out, ff_up, ff_down, norm1_weight, norm2_weight,
+                norm_q, norm_k, attention):
+        c = self.config = config
+        self.device = device
+        self.to_qkv, self.to_out, self.ff_up, self.ff_down = to_qkv, to_out, ff_up, ff_down
         # Gate-first SwiGLU fused into the up projection's epilogue when its
         # gate/value halves tile evenly (2F % 256 == 0).
         self.fused_swiglu = c.activation == "swiglu" and self.ff_up.out_features % 256 == 0
         if self.fused_swiglu:
             self.ff_up = self.ff_up.swiglu_interleaved()
-        self.ff_down = lin("ff_down")
-        self.norm1_weight = weights.get("norm1.weight")
-        self.norm2_weight = weights.get("norm2.weight")
-        if self.norm1_weight is not None:
-            self.norm1_weight = self.norm1_weight.to(device, torch.bfloat16)
-            self.norm2_weight = weights["norm2.weight"].to(device, torch.bfloat16)
-        self.norm_q = self.norm_k = None
-        if c.qk_norm:
-            self.norm_q = torch.nn.RMSNorm(c.head_dim, eps=c.eps).to(device, torch.bfloat16)
-            self.norm_k = torch.nn.RMSNorm(c.head_dim, eps=c.eps).to(device, torch.bfloat16)
-            self.norm_q.weight.data.copy_(weights["norm_q.weight"])
-            self.norm_k.weight.data.copy_(weights["norm_k.weight"])
-        self.attention = H3AttentionBackendB200(c.precision)
+        self.norm1_weight, self.norm2_weight = norm1_weight, norm2_weight
+        self.norm_q, self.norm_k = norm_q, norm_k
+        self.attention = attention
         self.parallel_manager = None
 
     def set_parallel_manager(self, parallel_manager) -> None:
@@ -106,7 +120,7 @@ class H3DiTBlockB200:
 
     def forward(self, x, adaln_table, adaln_indices, rotary_emb, *, sp_group=None, sp_size=1,
                 phaa_num=2, fp8_transport=True, comm_stream=None, pad_key="mmh3_seq",
-                parallel_manager=None):
+                parallel_manager=None, use_phaa=True):
         """x [B, S_loc, hidden] bf16 -> [B, S_loc, hidden] bf16. A
         `parallel_manager` (argument, else the `parallel_manager` attribute
         set_parallel_manager attaches) supplies the SP group and size, as the
@@ -134,12 +148,12 @@ class H3DiTBlockB200:
             att = sp_self_attention(q, k, v, rotary_emb, backend=self.attention, heads=c.heads,
                                     head_dim=c.head_dim, sp_group=sp_group, sp_size=sp_size,
                                     phaa_num=phaa_num, fp8_transport=fp8_transport,
-                                    comm_stream=comm_stream, pad_key=pad_key)
+                                    comm_stream=comm_stream, pad_key=pad_key, use_phaa=use_phaa)
             x = self.to_out.forward_gated(att, gate, idx, x)
             # feed-forward branch
             a, sa = norm_modulate_quant(x, c.norm, self.norm2_weight, c.eps, scale_ff, shift_ff, idx)
-            if c.activation == "gelu":
-                hid = self.ff_up.forward_quantized(a, sa, activation=1)
+            if c.activation in ("gelu", "gelu_tanh"):
+                hid = self.ff_up.forward_quantized(a, sa, activation=1 if c.activation == "gelu" else 2)
             elif self.fused_swiglu:
                 hid = self.ff_up.forward_quantized(a, sa, activation=3)
             else:

@@ -20,13 +20,16 @@ from ..sp.comm import all_to_all_after_attn, all_to_all_before_attn
 def sp_self_attention(query, key, value, rotary_emb, *, backend, heads: int, head_dim: int = 128,
                       sp_group=None, sp_size: int = 1, phaa_num: int = 2,
                       fp8_transport: bool = True, comm_stream=None, pad_key: str = "mmh3_seq",
-                      device_join: bool = True, use_phaa: bool = True, int8_transport: bool = False):
+                      device_join: bool = True, use_phaa: bool = True, int8_transport: bool = False,
+                      attention_mask=None):
     """query/key/value (B, S_loc, heads*head_dim) bf16 -> (B, S_loc, heads*head_dim).
     int8_transport: Sage-quantise before the exchange (xgen_b200.phaa.sage_wire)
-    and return the output over the FP8 wire."""
+    and return the output over the FP8 wire. attention_mask goes to the
+    backend, which takes its masked path for it (as the reference's
+    attention backends do)."""
     b, s, _ = query.shape
     with torch.no_grad():
-        if sp_size > 1 and int8_transport:
+        if sp_size > 1 and int8_transport and attention_mask is None:
             return run_phaa_attention(
                 query, key, value, comm_stream=comm_stream, sp_group=sp_group, sp_size=sp_size,
                 heads=heads, phaa_split_num=1, head_dim=head_dim, rotary_emb=rotary_emb,
@@ -40,7 +43,7 @@ def sp_self_attention(query, key, value, rotary_emb, *, backend, heads: int, hea
                 heads=heads, phaa_split_num=phaa_num, head_dim=head_dim,
                 rotary_emb=rotary_emb if fp8_transport else None, pad_key=pad_key,
                 attention_fn=backend, fp8_transport=fp8_transport, device_join=device_join,
-                fuse_rope=fp8_transport and rotary_emb is not None)
+                fuse_rope=fp8_transport and rotary_emb is not None, attention_mask=attention_mask)
         if rotary_emb is not None:
             query, key = _rope(query, key, rotary_emb, heads, head_dim)
         q4 = query.unflatten(-1, (heads, head_dim))
@@ -50,7 +53,7 @@ def sp_self_attention(query, key, value, rotary_emb, *, backend, heads: int, hea
             q4, k4, v4 = (all_to_all_before_attn(t, sp_group, 2, 1, pad_key) for t in (q4, k4, v4))
         out = torch.empty(q4.shape, device=q4.device, dtype=q4.dtype)
         res = backend(q4.transpose(1, 2), k4.transpose(1, 2), v4.transpose(1, 2),
-                      out=out.transpose(1, 2))
+                      attn_mask=attention_mask, out=out.transpose(1, 2))
         if res.data_ptr() != out.data_ptr():
             out.copy_(res.transpose(1, 2))
         if sp_size > 1:

@@ -138,8 +138,11 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
 
     # Sage backends take the received FP8 wire as it is: the Sage
     # preparation reads Q/K/V from it (bf16(e4m3 * scale), the decode's
-    # values), so there is no decode pass and no bf16 gather buffer.
+    # values), so there is no decode pass and no bf16 gather buffer. Only
+    # for bf16 activations: the wire decode rounds to the activation dtype,
+    # and the wire-reading preparation produces bf16 values.
     from_wire = (fp8_transport and not async_exchange and attention_mask is None
+                 and query.dtype == torch.bfloat16
                  and (rope_fn is None or rotary_emb is None or fuse_rope) and D == 128
                  and getattr(attention_fn, "precision", None) == "sage"
                  and hasattr(attention_fn, "attend_fp8_wire"))
