@@ -225,6 +225,16 @@ def hbm_kernels(args):
            f"3 x [1, {hl}, {SEQ}, 128] bf16 (gathered views)")
     del views, ws, gathered
 
+    # the SP = 1 path: RoPE fused into the preparation, [B, S, H, D] storage
+    full_cos, full_sin = (t.contiguous().to(dev) for t in rope_3d(GRID, TEXT + AUDIO))
+    qkv_seq = [rnd(1, SEQ, hl, HEAD_DIM).transpose(1, 2) for _ in range(3)]
+    ws = SageWorkspace(1, hl, SEQ, dev)
+    ms = timed(lambda: sage_prepare(*qkv_seq, ws=ws, rotary_emb=(full_cos, full_sin)))
+    record("sage_prep_rope", 3 * n * 2 + 2 * full_cos.numel() * 4 + 3 * n
+           + (2 * ws.q_scale.numel() + ws.v_scale.numel()) * 4, ms,
+           f"3 x [1, {SEQ}, {hl}, 128] bf16 + RoPE tables [{SEQ}, 128] fp32 (replaces RoPE + sage_prep)")
+    del qkv_seq, ws, full_cos, full_sin
+
     # standalone partial RoPE and Q/K RMSNorm + RoPE on [1, S_loc, H, D]
     q4, k4 = rnd(1, s_loc, HEADS, HEAD_DIM), rnd(1, s_loc, HEADS, HEAD_DIM)
     with torch.no_grad():
@@ -703,6 +713,17 @@ def main():
     value = FLOPS_PER_LAYER / (ms * 1e-3) / 1e12  # aggregate over all ranks
     # the timed layer's output at the sampled global rows (checked at the end)
     parity_got = gather_parity_rows(out, rank, world, s_loc, dev)
+    # and, at SP > 1 with Sage, one BF16 layer over the plain Ulysses
+    # all-to-all (bf16 both ways) on the same inputs, so both SP transports
+    # are checked on the hardware
+    ulysses_got = None
+    if world > 1 and args.precision == "sage":
+        bf16_backend = H3AttentionBackendB200("bf16")
+        bf16_out = sp_self_attention(q, k, v, (cos, sin), backend=bf16_backend, heads=HEADS,
+                                     head_dim=HEAD_DIM, sp_group=group, sp_size=world,
+                                     use_phaa=False, fp8_transport=False)
+        ulysses_got = gather_parity_rows(bf16_out, rank, world, s_loc, dev)
+        del bf16_out
 
     # ---- dominant kernel alone: the attention kernel on prepared inputs
     roof = attention_roofline(args.precision, world, dev, s_pad)
@@ -744,6 +765,10 @@ def main():
         wire = None if world == 1 or args.precision != "sage" else args.wire
         ref, exact = reference_rows(args.precision, wire, dev, cos_full, sin_full)
         parity = parity_summary(parity_got, ref, exact, args.precision, wire, world)
+        if ulysses_got is not None:
+            parity["ulysses_bf16"] = parity_summary(ulysses_got, exact, exact, "bf16", None, world)
+            parity["ulysses_bf16"]["reference"] = ("fp64 SDPA of the same RoPE'd global inputs; "
+                                                   "one BF16 layer over the plain Ulysses all-to-all")
         del ref, exact
         torch.cuda.empty_cache()
     barrier()
@@ -894,17 +919,21 @@ def c5_timing(args, world, rank, dev, group, comm_stream, barrier, max_over_rank
 
 
 def kernels_per_step(precision, world, phaa, wire="fp8"):
-    """Our kernel launches per layer: SP=1: RoPE + (Sage: 3 prepare + 1 attention).
-    SP>1 per PHAA chunk: QKV encode, decode, (Sage: 3 prepare) + attention,
-    return encode, decode. INT8 wire (one chunk): stats, stats finalize,
-    encode, attention, return encode, decode."""
-    attn = 4 if precision == "sage" else 1
+    """Our kernel launches per layer.
+    SP = 1: Sage: statistics + quantisation (RoPE fused in) + attention; BF16:
+    RoPE + attention.
+    SP > 1, Sage over the FP8 wire, per PHAA chunk: QKV encode (RoPE fused),
+    statistics + quantisation read from the received wire, attention, return
+    encode, return decode. BF16: RoPE, then per chunk the attention (the
+    Ulysses exchange is NCCL's). INT8 wire (one chunk): statistics, statistics
+    finalize, encode, attention, return encode, decode."""
     if world == 1:
-        return 1 + attn
+        return 3 if precision == "sage" else 2
     if precision == "sage" and wire == "int8":
         return 6
-    per_chunk = attn + (4 if precision == "sage" else 0)
-    return phaa * per_chunk + (1 if precision != "sage" else 0)
+    if precision == "sage":
+        return 6 * phaa
+    return 1 + phaa
 
 
 def attention_roofline(precision, world, dev, s_pad):

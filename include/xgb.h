@@ -259,6 +259,22 @@ int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void* k,
                      int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
                      float* v_scale, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* xgb_sage_prepare of bf16 Q/K/V with the rotate-half RoPE of the first
+ * `rotary` channels of Q and K applied as they are read (rotary a multiple
+ * of 16, <= 128): cos/sin fp32 [seq, rotary] (16-byte aligned rows of the
+ * attention's sequence positions); each rotated value is
+ * bf16(bf16(x*bf16(cos)) + bf16(+-partner*bf16(sin))), the reference's
+ * rounding. Replaces `try_h3_partial_rope` (x_base/x_base/operator/
+ * h3_partial_rope.py:9-47) followed by the quantisation inside `sageattn`
+ * (x_base/x_base/operator/attention.py:363-375); the outputs equal
+ * xgb_partial_rope + xgb_sage_prepare. Same workspace as xgb_sage_prepare. */
+int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const void* k,
+                          const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                          int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, float sm_scale,
+                          const float* cos, const float* sin, int64_t rotary, int8_t* q8,
+                          float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8, float* v_scale,
+                          void* workspace, int64_t workspace_bytes, void* stream);
+
 /* xgb_sage_prepare reading Q/K/V straight from a received PHAA FP8 wire
  * (the payload fp8_all_to_all_many exchanges, x_base/x_base/phaa/
  * fp8_transport.py:85-144, before its decode): per source peer p the Q, K

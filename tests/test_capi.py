@@ -68,6 +68,28 @@ def test_argument_errors_without_gpu():
     assert prep(*ok[:14], dummy, 16, None) == -7                       # workspace too small
 
 
+def test_fused_rope_prepare_argument_errors_without_gpu():
+    """xgb_sage_prepare_rope rejects bad RoPE widths, strides, alignment and
+    a short workspace before any CUDA call."""
+    from xgen_b200 import _lib
+
+    h = _lib.lib()
+    d = ctypes.c_void_p(1 << 20)  # 16-byte aligned stand-in pointer (never dereferenced)
+    st = _lib.i64_array([300 * 2 * 128, 128, 2 * 128, 1])
+    f = ctypes.c_float(0.088)
+
+    def call(*, cos=d, rotary=96, strides=st, ws_bytes=1 << 30, q=d):
+        return h.xgb_sage_prepare_rope(q, strides, d, strides, d, strides, 1, 2, 300, 128, f, cos, d,
+                                       rotary, d, d, d, d, d, d, d, ws_bytes, None)
+
+    assert call(q=None) == -1                                  # null input
+    assert call(rotary=90) == -2                               # rotary/2 not a multiple of 8
+    assert call(rotary=144) == -2                              # wider than the head
+    assert call(strides=_lib.i64_array([300 * 256, 128, 256, 2])) == -3  # channel stride
+    assert call(cos=ctypes.c_void_p((1 << 20) + 4)) == -4      # cos table not 16-byte aligned
+    assert call(ws_bytes=16) == -7                             # workspace too small
+
+
 def test_ops_refuse_cpu_tensors():
     torch = pytest.importorskip("torch")
     from xgen_b200 import ops

@@ -48,6 +48,59 @@ def test_sage_prepare_vs_oracle(cuda_device):
     assert not ws.q8[:, s:].any() and not ws.k8[:, s:].any() and not ws.v8[:, s:].any()
 
 
+@pytest.mark.parametrize("b,h,s,rotary,transposed", [(1, 2, 300, 96, False), (2, 3, 1000, 128, True),
+                                                     (1, 1, 4097, 64, False)])
+def test_sage_prepare_with_rope_equals_rope_then_prepare(cuda_device, b, h, s, rotary, transposed):
+    """xgb_sage_prepare_rope (RoPE applied as Q/K are read) gives the same
+    bytes as the RoPE kernel followed by xgb_sage_prepare, and the RoPE'd
+    values equal the oracle's restatement of h3_partial_rope.py:9-29."""
+    from oracle import elementwise as ew
+    from xgen_b200.attention import SageWorkspace, sage_prepare
+    from xgen_b200.h3.rope import rope_partial
+    from xgen_b200.ops import try_h3_partial_rope
+
+    q, k, v = make_qkv(b, h, s, seed=3)
+    cos, sin = rope_partial(s, rotary)
+    dev = cuda_device
+    if transposed:  # [B, S, H, D] storage seen as [B, H, S, D] views, as sp_self_attention passes
+        q, k, v = (t.transpose(1, 2).contiguous().to(dev).transpose(1, 2) for t in (q, k, v))
+    else:
+        q, k, v = (t.to(dev) for t in (q, k, v))
+    cs = (cos.to(dev), sin.to(dev))
+    fused = sage_prepare(q, k, v, ws=SageWorkspace(b, h, s, dev), rotary_emb=cs)
+    with torch.no_grad():  # the try_* ops decline under autograd, as the reference's do
+        q4, k4 = try_h3_partial_rope(q.transpose(1, 2).contiguous(), k.transpose(1, 2).contiguous(), *cs)
+    qr, kr = q4.transpose(1, 2), k4.transpose(1, 2)
+    plain = sage_prepare(qr, kr, v, ws=SageWorkspace(b, h, s, dev))
+    for name in ("q8", "k8", "v8", "q_scale", "k_scale", "v_scale"):
+        assert torch.equal(getattr(fused, name), getattr(plain, name)), name
+    eq, ek = ew.partial_rope(to_np(q.transpose(1, 2)), to_np(k.transpose(1, 2)), cos.numpy(), sin.numpy())
+    np.testing.assert_array_equal(to_np(q4), eq)
+    np.testing.assert_array_equal(to_np(k4), ek)
+
+
+def test_sage_backend_fuses_rope_at_sp1(cuda_device):
+    """sp_self_attention at SP = 1 hands the RoPE to the Sage backend (no
+    RoPE kernel of its own): same output as RoPE first, then attention."""
+    from xgen_b200.attention import H3AttentionBackendB200
+    from xgen_b200.h3.rope import rope_partial
+    from xgen_b200.h3.sp_attention import sp_self_attention
+    from xgen_b200.ops import try_h3_partial_rope
+
+    g = torch.Generator().manual_seed(8)
+    s, heads = 700, 2
+    q, k, v = (torch.randn(1, s, heads * 128, generator=g).bfloat16().to(cuda_device) for _ in range(3))
+    cos, sin = (t.to(cuda_device) for t in rope_partial(s, 96))
+    backend = H3AttentionBackendB200("sage")
+    assert backend.fuses_rope(q)
+    with torch.no_grad():
+        got = sp_self_attention(q, k, v, (cos, sin), backend=backend, heads=heads)
+        q4, k4 = try_h3_partial_rope(q.unflatten(-1, (heads, 128)), k.unflatten(-1, (heads, 128)), cos, sin)
+        expect = sp_self_attention(q4.flatten(2), k4.flatten(2), v, None, backend=backend, heads=heads)
+    torch.cuda.synchronize()
+    assert torch.equal(got, expect)
+
+
 @pytest.mark.parametrize("b,h,s", [(1, 1, 128), (1, 2, 300), (2, 3, 1000), (1, 1, 4097)])
 def test_sage_attention_vs_oracle(cuda_device, b, h, s):
     from xgen_b200.attention import kernel_errors, sage_attention

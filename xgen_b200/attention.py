@@ -101,9 +101,12 @@ class SageWorkspace:
         self.scratch_bytes = nbytes
 
 
-def sage_prepare(q, k, v, sm_scale: float | None = None, ws: SageWorkspace | None = None):
+def sage_prepare(q, k, v, sm_scale: float | None = None, ws: SageWorkspace | None = None,
+                 rotary_emb=None):
     """Sage quantisation of bf16/fp16 [B, H, S, 128] views: K mean-smoothing,
-    per-64-token INT8 Q (sm_scale*log2e folded in) and K, per-channel e4m3 V."""
+    per-64-token INT8 Q (sm_scale*log2e folded in) and K, per-channel e4m3 V.
+    rotary_emb=(cos, sin) (fp32 [S, R], bf16 inputs): the rotate-half RoPE
+    of Q and K is applied inside the same kernels (xgb_sage_prepare_rope)."""
     _check_qkv(q, k, v, "Sage attention")
     if q.shape != k.shape:
         raise ValueError("Sage attention expects self-attention shapes (Sq == Skv)")
@@ -114,6 +117,18 @@ def sage_prepare(q, k, v, sm_scale: float | None = None, ws: SageWorkspace | Non
     dtype = {torch.bfloat16: _lib.XGB_BF16, torch.float16: _lib.XGB_F16}.get(q.dtype)
     if dtype is None or k.dtype != q.dtype or v.dtype != q.dtype:
         raise ValueError("Sage attention requires bf16/fp16 inputs of one dtype")
+    if rotary_emb is not None:
+        cos, sin = rotary_emb
+        if (q.dtype != torch.bfloat16 or cos.dtype != torch.float32 or sin.dtype != torch.float32
+                or cos.shape != sin.shape or cos.ndim != 2 or cos.shape[0] != s or not cos.is_cuda
+                or not cos.is_contiguous() or not sin.is_contiguous()):
+            raise ValueError("fused Sage RoPE needs bf16 Q/K/V and contiguous fp32 cos/sin [S, R] on the GPU")
+        call("xgb_sage_prepare_rope", q.data_ptr(), i64_array(q.stride()), k.data_ptr(),
+             i64_array(k.stride()), v.data_ptr(), i64_array(v.stride()), b, h, s, d, sm_scale,
+             cos.data_ptr(), sin.data_ptr(), cos.shape[1], ws.q8.data_ptr(), ws.q_scale.data_ptr(),
+             ws.k8.data_ptr(), ws.k_scale.data_ptr(), ws.v8.data_ptr(), ws.v_scale.data_ptr(),
+             ws.scratch.data_ptr(), ws.scratch_bytes, _stream(q))
+        return ws
     call("xgb_sage_prepare", q.data_ptr(), i64_array(q.stride()), k.data_ptr(),
          i64_array(k.stride()), v.data_ptr(), i64_array(v.stride()), dtype, b, h, s, d, sm_scale,
          ws.q8.data_ptr(), ws.q_scale.data_ptr(), ws.k8.data_ptr(), ws.k_scale.data_ptr(),
@@ -159,9 +174,10 @@ def sage_attention_prepared(ws: SageWorkspace, out: torch.Tensor | None = None) 
 
 
 def sage_attention(q, k, v, sm_scale: float | None = None, out=None,
-                   ws: SageWorkspace | None = None) -> torch.Tensor:
-    """Sage-style quantised attention of bf16 [B, H, S, 128] views (HND)."""
-    ws = sage_prepare(q, k, v, sm_scale, ws)
+                   ws: SageWorkspace | None = None, rotary_emb=None) -> torch.Tensor:
+    """Sage-style quantised attention of bf16 [B, H, S, 128] views (HND);
+    rotary_emb: RoPE fused into the preparation (see sage_prepare)."""
+    ws = sage_prepare(q, k, v, sm_scale, ws, rotary_emb=rotary_emb)
     return sage_attention_prepared(ws, out)
 
 
@@ -224,9 +240,20 @@ class H3AttentionBackendB200:
         self.calls += 1
         return out
 
-    def __call__(self, query, key, value, *, attn_mask=None, head_offset=0, out=None):
-        if self._kernel_eligible(query, key, value, attn_mask) and (
-                out is None or query.dtype == torch.bfloat16):
+    def fuses_rope(self, query) -> bool:
+        """Whether a call with `rotary_emb` applies the RoPE inside the Sage
+        preparation (bf16 Sage) rather than as a pass of its own."""
+        return self.precision == "sage" and query.dtype == torch.bfloat16
+
+    def __call__(self, query, key, value, *, attn_mask=None, head_offset=0, out=None, rotary_emb=None):
+        """B200 extension: `rotary_emb=(cos, sin)` (fp32 [S, R] over the
+        sequence positions) rotates Q and K first, fused into the Sage
+        preparation when `fuses_rope(query)`."""
+        eligible = self._kernel_eligible(query, key, value, attn_mask) and (
+            out is None or query.dtype == torch.bfloat16)
+        if rotary_emb is not None and not (eligible and self.fuses_rope(query)):
+            query, key = _rope_heads_major(query, key, rotary_emb)
+        if eligible:
             if self.precision == "sage":
                 b, h, s, _ = query.shape
                 key_ = (b, h, s, query.device)
@@ -234,7 +261,8 @@ class H3AttentionBackendB200:
                     self._ws = {}
                 if key_ not in self._ws:
                     self._ws[key_] = SageWorkspace(b, h, s, query.device)
-                output = sage_attention(query, key, value, out=out, ws=self._ws[key_])
+                output = sage_attention(query, key, value, out=out, ws=self._ws[key_],
+                                        rotary_emb=rotary_emb)
             else:
                 output = dense_attention(query, key, value, out=out)
             self.kernel_calls += 1
@@ -246,3 +274,17 @@ class H3AttentionBackendB200:
                 output = out
         self.calls += 1
         return output
+
+
+def _rope_heads_major(query, key, rotary_emb):
+    """Rotate-half RoPE of [B, H, S, D] Q/K views with the B200 kernel
+    (which takes [B, S, H, D] rows)."""
+    from .ops import try_h3_partial_rope
+
+    q4 = query.transpose(1, 2).contiguous()
+    k4 = key.transpose(1, 2).contiguous()
+    with torch.no_grad():  # the kernels carry no autograd
+        rotated = try_h3_partial_rope(q4, k4, *rotary_emb)
+    if rotated is None:
+        raise ValueError("H3 RoPE tables must be fp32 [S, R] with even R <= head_dim")
+    return rotated[0].transpose(1, 2), rotated[1].transpose(1, 2)

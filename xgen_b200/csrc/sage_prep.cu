@@ -11,8 +11,12 @@
 // S_pad = roundup(S, 128); rows >= S are zero. Scales fp32: q/k
 // [B*H][S_pad/64], v [B*H][128].
 //
-// Three launches: per-chunk K sums and V abs-max (partials in the caller's
-// workspace), a per-head finalize (mean, V scale), and the block quantiser.
+// Two launches: per-chunk K sums and V abs-max (partials in the caller's
+// workspace; the last chunk of a head to finish turns them into the K mean
+// and the V scale), then the block quantiser. `xgb_sage_prepare_rope` also
+// applies the rotate-half RoPE of Q and K (x_base/x_base/operator/
+// h3_partial_rope.py:9-29) as it loads them, so the RoPE needs no pass of
+// its own.
 #include <cfloat>
 
 #include "xgb_common.cuh"
@@ -37,11 +41,14 @@ struct Strides {
 };
 
 // Workspace: ksum partials [BH][chunks][128] fp32, vmax [BH][128] int,
+// done [BH] int (chunks of the head finished; zeroed with vmax per call),
 // kmean [BH][128] fp32.
 struct Workspace {
   float* ksum;
   int* vmax;
+  int* done;
   float* kmean;
+  float* vscale;  // the caller's v_scale output
 };
 
 inline int64_t stats_chunks(int64_t seq) { return (seq + kStatsRows - 1) / kStatsRows; }
@@ -53,6 +60,8 @@ inline Workspace carve(void* ws, int64_t bh, int64_t chunks) {
   p += bh * chunks * kD * sizeof(float);
   w.vmax = reinterpret_cast<int*>(p);
   p += bh * kD * sizeof(int);
+  w.done = reinterpret_cast<int*>(p);
+  p += (bh + 3) / 4 * 4 * sizeof(int);
   w.kmean = reinterpret_cast<float*>(p);
   return w;
 }
@@ -81,6 +90,31 @@ struct StridedSource {
   }
   __device__ __forceinline__ static Raw zero() { return make_uint4(0, 0, 0, 0); }
   __device__ __forceinline__ static void unpack(const Raw& r, float (&x)[8]) { unpack8<T>(r, x); }
+};
+
+// RopeSource: bf16 [B, H, S, 128] views like StridedSource, with the
+// rotate-half RoPE of the first `rotary` channels applied to Q (stream 0)
+// and K (stream 1) as they are loaded: channel c pairs with c +- rotary/2
+// (the partner chunk is a second 16-byte load of the same row), and each
+// product and the sum round to bf16, the reference's arithmetic (rope8_bf16).
+// cos/sin: fp32 [S, rotary] rows of the attention's sequence positions.
+struct RopeSource {
+  StridedSource<__nv_bfloat16> base;
+  const float* cos;
+  const float* sin;
+  int rotary;
+  using Raw = uint4;
+  __device__ __forceinline__ Raw load(int stream, int64_t b, int64_t h, int64_t row, int c0) const {
+    const Raw x = base.load(stream, b, h, row, c0);
+    if (stream == 2 || c0 >= rotary) return x;
+    const int half = rotary / 2;
+    const bool first = c0 < half;
+    const Raw partner = base.load(stream, b, h, row, first ? c0 + half : c0 - half);
+    const int64_t at = row * rotary + c0;
+    return rope8_bf16(x, partner, first, cos + at, sin + at);
+  }
+  __device__ __forceinline__ static Raw zero() { return make_uint4(0, 0, 0, 0); }
+  __device__ __forceinline__ static void unpack(const Raw& r, float (&x)[8]) { unpack8<__nv_bfloat16>(r, x); }
 };
 
 // WireSource: the received PHAA FP8 wire (x_base/x_base/phaa/fp8_transport.py
@@ -122,15 +156,19 @@ struct WireSource {
 
 // Per 512-row chunk of one head: channel sums of K and channel abs-max of V.
 // Thread t owns channels 8*(t%16)..+8 of rows t/16 + 16*i.
+// Grids of both kernels put (batch, head) fastest: consecutive CTAs read the
+// same sequence rows of all heads (contiguous in [B, S, H, D] storage and on
+// the wire, and sharing the RoPE table rows in L2).
 template <typename Src>
 __global__ void __launch_bounds__(kThreads) stats_kernel(Src src, int64_t heads, int64_t seq,
                                                          Workspace w, int64_t chunks) {
-  const int64_t bh = blockIdx.y;
+  const int64_t bh = blockIdx.x;
+  const int64_t chunk = blockIdx.y;
   const int64_t b = bh / heads, h = bh % heads;
   const int cg = threadIdx.x % 16;
   const int rr = threadIdx.x / 16;
   const int c0 = cg * 8;
-  const int64_t row_begin = static_cast<int64_t>(blockIdx.x) * kStatsRows;
+  const int64_t row_begin = chunk * kStatsRows;
   const int64_t row_end = min(row_begin + kStatsRows, seq);
   float sum[8], vmx[8];
 #pragma unroll
@@ -164,35 +202,38 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(Src src, int64_t heads,
       t += part[i][c];
       m = fmaxf(m, vpart[i][c]);
     }
-    w.ksum[(bh * chunks + blockIdx.x) * kD + c] = t;
+    w.ksum[(bh * chunks + chunk) * kD + c] = t;
     atomicMax(&w.vmax[bh * kD + c], __float_as_int(m));
   }
-}
-
-// Per head: K channel means from the chunk partials and the V channel
-// scales. Eight slices of 128 threads each sum every eighth chunk, then the
-// slices are added in a fixed order (deterministic; 1,024 threads per head
-// instead of one serial pass per channel).
-constexpr int kFinalSlices = 8;
-
-__global__ void __launch_bounds__(kD* kFinalSlices) finalize_kernel(Workspace w, int64_t chunks,
-                                                                    int64_t seq,
-                                                                    float* __restrict__ v_scale) {
-  const int64_t bh = blockIdx.x;
-  const int c = threadIdx.x % kD;
-  const int slice = threadIdx.x / kD;
-  __shared__ float part[kFinalSlices][kD];
-  float sum = 0.f;
-  for (int64_t i = slice; i < chunks; i += kFinalSlices) sum += w.ksum[(bh * chunks + i) * kD + c];
-  part[slice][c] = sum;
+  // The last chunk of the head to finish turns the partials into the K
+  // channel means and the V channel scales: eight slices each sum every
+  // eighth chunk, then the slices are added in a fixed order, so the result
+  // does not depend on which chunk finishes last.
+  __threadfence();
   __syncthreads();
-  if (slice == 0) {
+  __shared__ int last;
+  if (threadIdx.x == 0) last = atomicAdd(&w.done[bh], 1) == chunks - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  constexpr int kSlices = 8;
+  float* slices = &part[0][0];  // reuse: kSlices x kD floats fit in part
+  static_assert(kSlices * kD <= (kThreads / 16) * kD, "slice scratch");
+  for (int k = threadIdx.x; k < kSlices * kD; k += kThreads) {
+    const int c = k % kD, slice = k / kD;
+    float sum = 0.f;
+    for (int64_t i = slice; i < chunks; i += kSlices) sum += __ldcg(&w.ksum[(bh * chunks + i) * kD + c]);
+    slices[slice * kD + c] = sum;
+  }
+  __syncthreads();
+  if (threadIdx.x < kD) {
+    const int c = threadIdx.x;
     float t = 0.f;
 #pragma unroll
-    for (int j = 0; j < kFinalSlices; ++j) t += part[j][c];
+    for (int j = 0; j < kSlices; ++j) t += slices[j * kD + c];
     w.kmean[bh * kD + c] = __fdiv_rn(t, static_cast<float>(seq));
-    const float sc = __fdiv_rn(__int_as_float(w.vmax[bh * kD + c]), 448.0f);
-    v_scale[bh * kD + c] = fmaxf(sc, FLT_MIN);
+    const float sc = __fdiv_rn(__int_as_float(__ldcg(&w.vmax[bh * kD + c])), 448.0f);
+    w.vscale[bh * kD + c] = fmaxf(sc, FLT_MIN);
   }
 }
 
@@ -245,9 +286,9 @@ __global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
     Src src, int64_t heads, int64_t seq, int64_t s_pad, float q_mult, Workspace w,
     const float* __restrict__ v_scale, int8_t* __restrict__ q8, float* __restrict__ q_scale,
     int8_t* __restrict__ k8, float* __restrict__ k_scale, uint8_t* __restrict__ v8) {
-  const int64_t bh = blockIdx.y;
+  const int64_t bh = blockIdx.x;
   const int64_t b = bh / heads, h = bh % heads;
-  const int64_t blk = blockIdx.x;
+  const int64_t blk = blockIdx.y;
   const int cg = threadIdx.x % 16;
   const int rr = threadIdx.x / 16;
   const int c0 = cg * 8;
@@ -342,7 +383,7 @@ struct Outputs {
 };
 
 inline int64_t stats_workspace(int64_t bh, int64_t seq) {
-  return bh * stats_chunks(seq) * kD * 4 + bh * kD * 4 + bh * kD * 4;
+  return bh * stats_chunks(seq) * kD * 4 + bh * kD * 4 + (bh + 3) / 4 * 4 * 4 + bh * kD * 4;
 }
 
 // Statistics, finalize and quantisation of [batch, heads, seq] rows read from `src`.
@@ -353,12 +394,15 @@ int prepare(const Src& src, int64_t batch, int64_t heads, int64_t seq, float sm_
   const int64_t chunks = stats_chunks(seq);
   const int64_t s_pad = (seq + 127) / 128 * 128;
   Workspace w = carve(workspace, bh, chunks);
-  if (cudaMemsetAsync(w.vmax, 0, bh * kD * sizeof(int), st) != cudaSuccess) return XGB_ERR_LAUNCH;
+  w.vscale = o.v_scale;
+  // vmax and the per-head chunk counters, contiguous
+  const size_t zero_bytes = bh * kD * sizeof(int) + (bh + 3) / 4 * 4 * sizeof(int);
+  if (cudaMemsetAsync(w.vmax, 0, zero_bytes, st) != cudaSuccess) return XGB_ERR_LAUNCH;
   const float q_mult = sm_scale * kLog2e;
-  const dim3 sgrid(static_cast<unsigned>(chunks), static_cast<unsigned>(bh));
-  const dim3 qgrid(static_cast<unsigned>(s_pad / 64), static_cast<unsigned>(bh));
+  if (chunks > 65535 || s_pad / 64 > 65535) return XGB_ERR_SHAPE;  // grid y
+  const dim3 sgrid(static_cast<unsigned>(bh), static_cast<unsigned>(chunks));
+  const dim3 qgrid(static_cast<unsigned>(bh), static_cast<unsigned>(s_pad / 64));
   stats_kernel<<<sgrid, kThreads, 0, st>>>(src, heads, seq, w, chunks);
-  finalize_kernel<<<static_cast<unsigned>(bh), kD * kFinalSlices, 0, st>>>(w, chunks, seq, o.v_scale);
   quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(src, heads, seq, s_pad, q_mult, w, o.v_scale, o.q8,
                                                 o.q_scale, o.k8, o.k_scale, o.v8);
   return launch_status();
@@ -411,6 +455,45 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
   using S = StridedSource<__half>;
   const S src{{static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v)},
               {qs, ks, vs}};
+  return prepare(src, batch, heads, seq, sm_scale, o, workspace, as_stream(stream));
+}
+
+XGB_API int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const void* k,
+                                  const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                                  int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                                  float sm_scale, const float* cos, const float* sin, int64_t rotary,
+                                  int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
+                                  float* v_scale, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
+  if (!q || !k || !v || !q_strides || !k_strides || !v_strides || !cos || !sin) return XGB_ERR_ARG;
+  if (!q8 || !q_scale || !k8 || !k_scale || !v8 || !v_scale) return XGB_ERR_ARG;
+  if (head_dim != kD) return XGB_ERR_SHAPE;
+  if (batch <= 0 || heads <= 0 || seq <= 0) return XGB_ERR_SHAPE;
+  // 8-channel chunks pair with chunks rotary/2 away: rotary/2 a multiple of 8
+  if (rotary <= 0 || rotary > kD || rotary % 16) return XGB_ERR_SHAPE;
+  if (!(sm_scale > 0.f)) return XGB_ERR_ARG;
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1) return XGB_ERR_STRIDE;
+  for (int d = 0; d < 3; ++d)
+    if (q_strides[d] % 8 || k_strides[d] % 8 || v_strides[d] % 8) return XGB_ERR_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) & 15u)
+    return XGB_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(q8) | reinterpret_cast<uintptr_t>(k8) |
+       reinterpret_cast<uintptr_t>(v8)) & 15u)
+    return XGB_ERR_ALIGN;
+  const int64_t need = xgb_sage_prepare_workspace(batch, heads, seq);
+  if (!workspace || workspace_bytes < need) return XGB_ERR_WORKSPACE;
+  using B = StridedSource<__nv_bfloat16>;
+  RopeSource src{};
+  src.base = B{{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                static_cast<const __nv_bfloat16*>(v)},
+               {Strides{q_strides[0], q_strides[1], q_strides[2]},
+                Strides{k_strides[0], k_strides[1], k_strides[2]},
+                Strides{v_strides[0], v_strides[1], v_strides[2]}}};
+  src.cos = cos;
+  src.sin = sin;
+  src.rotary = static_cast<int>(rotary);
+  const Outputs o{q8, q_scale, k8, k_scale, v8, v_scale};
   return prepare(src, batch, heads, seq, sm_scale, o, workspace, as_stream(stream));
 }
 

@@ -4,9 +4,9 @@
 (x_diffusers/x_diffusers/framework/transformer/minimax_h3.py:165-247) that
 runs after Q/K normalisation: partial RoPE, the Ulysses/PHAA redistribution
 when SP > 1, the attention backend, and the return redistribution. With the
-FP8 wire the RoPE is fused into the wire encode; at SP = 1 it runs as the
-standalone RoPE kernel and the backend writes straight into the (B, S, H, D)
-output.
+FP8 wire the RoPE is fused into the wire encode; at SP = 1 a Sage backend
+applies it inside its quantisation kernels (a standalone RoPE kernel runs
+otherwise), and the backend writes straight into the (B, S, H, D) output.
 """
 from __future__ import annotations
 
@@ -44,7 +44,9 @@ def sp_self_attention(query, key, value, rotary_emb, *, backend, heads: int, hea
                 rotary_emb=rotary_emb if fp8_transport else None, pad_key=pad_key,
                 attention_fn=backend, fp8_transport=fp8_transport, device_join=device_join,
                 fuse_rope=fp8_transport and rotary_emb is not None, attention_mask=attention_mask)
-        if rotary_emb is not None:
+        fuse = (rotary_emb is not None and sp_size == 1 and attention_mask is None
+                and callable(getattr(backend, "fuses_rope", None)) and backend.fuses_rope(query))
+        if rotary_emb is not None and not fuse:
             query, key = _rope(query, key, rotary_emb, heads, head_dim)
         q4 = query.unflatten(-1, (heads, head_dim))
         k4 = key.unflatten(-1, (heads, head_dim))
@@ -52,8 +54,9 @@ def sp_self_attention(query, key, value, rotary_emb, *, backend, heads: int, hea
         if sp_size > 1:
             q4, k4, v4 = (all_to_all_before_attn(t, sp_group, 2, 1, pad_key) for t in (q4, k4, v4))
         out = torch.empty(q4.shape, device=q4.device, dtype=q4.dtype)
+        extra = {"rotary_emb": rotary_emb} if fuse else {}
         res = backend(q4.transpose(1, 2), k4.transpose(1, 2), v4.transpose(1, 2),
-                      attn_mask=attention_mask, out=out.transpose(1, 2))
+                      attn_mask=attention_mask, out=out.transpose(1, 2), **extra)
         if res.data_ptr() != out.data_ptr():
             out.copy_(res.transpose(1, 2))
         if sp_size > 1:
