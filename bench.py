@@ -58,6 +58,9 @@ def parse():
     # one-CTA-per-SM attention kernel slow it more than they hide, and
     # chunks of 3 heads quantize to 10.05 waves of 148 SMs.
     ap.add_argument("--phaa-num", type=int, default=1)
+    ap.add_argument("--nccl-max-ctas", type=int, default=0,
+                    help="cap the CTAs of the SP exchange's NCCL communicator (0: NCCL's default), "
+                         "so the exchanges of overlapped PHAA chunks take few SMs from the attention")
     ap.add_argument("--wire", choices=("fp8", "int8"), default="fp8",
                     help="SP gather transport (Sage): the FP8 wire, or Sage-quantised INT8")
     ap.add_argument("--no-e2e", action="store_true")
@@ -693,6 +696,13 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
         # the H3 enable_parallel mesh: every GPU of the job in one SP group
         group = ParallelManager(1, 1, world, 1).sp_group
+        if args.nccl_max_ctas > 0:
+            # the same ranks, on a communicator whose kernels use at most
+            # --nccl-max-ctas CTAs (collective: every rank creates it)
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.config.max_ctas = args.nccl_max_ctas
+            opts.config.min_ctas = 1
+            group = dist.new_group(dist.get_process_group_ranks(group), pg_options=opts)
     _lib.lib()
 
     # Workload: under SP the packed sequence is padded to a multiple of 16*SP
