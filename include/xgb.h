@@ -239,7 +239,8 @@ int xgb_norm_modulate_quant(const void* x, int64_t ldx, int64_t rows, int64_t wi
 
 /* ---- Attention (tcgen05 / TMEM / TMA kernels) ---- */
 
-/* Bytes of workspace xgb_sage_prepare needs. */
+/* Bytes of workspace xgb_sage_prepare needs (16-byte aligned; its contents
+ * need no initialisation). */
 int64_t xgb_sage_prepare_workspace(int64_t batch, int64_t heads, int64_t seq);
 
 /* Sage quantisation of post-A2A Q/K/V views [batch, heads, seq, head_dim]
@@ -250,6 +251,10 @@ int64_t xgb_sage_prepare_workspace(int64_t batch, int64_t heads, int64_t seq);
  * Outputs (16-byte aligned): q8/k8/v8 [batch*heads][S_pad][128] with
  * S_pad = roundup(seq, 128) (rows >= seq zero), q_scale/k_scale
  * [batch*heads][S_pad/64], v_scale [batch*heads][128].
+ * One cooperative kernel launch (one or two CTAs per SM) reads Q, K and V
+ * once, quantises Q and gathers the K/V statistics, then quantises K and V;
+ * its grid barriers give up after 2 s and record a timeout in *error_flag
+ * (device int, may be NULL), as the attention kernels do.
  * Replaces the quantisation inside `sageattn` as called at
  * x_base/x_base/operator/attention.py:363-375 (SageAttention 2.2.0, not in
  * the reference tree; algorithm per the SageAttention2 paper). */
@@ -257,7 +262,8 @@ int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void* k,
                      const int64_t* k_strides, const void* v, const int64_t* v_strides, int dtype,
                      int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, float sm_scale,
                      int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
-                     float* v_scale, void* workspace, int64_t workspace_bytes, void* stream);
+                     float* v_scale, void* workspace, int64_t workspace_bytes, int* error_flag,
+                     void* stream);
 
 /* xgb_sage_prepare of bf16 Q/K/V with the rotate-half RoPE of the first
  * `rotary` channels of Q and K applied as they are read (rotary a multiple
@@ -273,7 +279,7 @@ int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const void* k
                           int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, float sm_scale,
                           const float* cos, const float* sin, int64_t rotary, int8_t* q8,
                           float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8, float* v_scale,
-                          void* workspace, int64_t workspace_bytes, void* stream);
+                          void* workspace, int64_t workspace_bytes, int* error_flag, void* stream);
 
 /* xgb_sage_prepare reading Q/K/V straight from a received PHAA FP8 wire
  * (the payload fp8_all_to_all_many exchanges, x_base/x_base/phaa/
@@ -287,7 +293,8 @@ int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const void* k
 int xgb_sage_prepare_wire(const uint8_t* payload, int64_t peers, int64_t seq, int64_t batch,
                           int64_t heads, int64_t valid_seq, int64_t peer_padding, float sm_scale,
                           int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
-                          float* v_scale, void* workspace, int64_t workspace_bytes, void* stream);
+                          float* v_scale, void* workspace, int64_t workspace_bytes, int* error_flag,
+                          void* stream);
 
 /* Non-causal attention over xgb_sage_prepare's outputs: INT8 Q.K^T
  * (tcgen05 kind::i8), fp32 online softmax in the exp2 domain, e4m3 P.V

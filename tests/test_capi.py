@@ -60,12 +60,12 @@ def test_argument_errors_without_gpu():
     # Sage preparation from the FP8 wire: pointers, layout and alignment
     prep = lambda *a: h.xgb_sage_prepare_wire(*a)  # noqa: E731
     ok = (dummy, 2, 64, 1, 3, 100, 0, ctypes.c_float(0.088), dummy, dummy, dummy, dummy, dummy, dummy,
-          dummy, 1 << 20, None)
+          dummy, 1 << 20, None, None)
     assert prep(None, *ok[1:]) == -1                                   # null payload
     assert prep(*ok[:5], 129, *ok[6:]) == -2                           # valid_seq > peers * seq
     assert prep(*ok[:6], 2, *ok[7:]) == -1                             # padding not a multiple of 4
     assert prep(ctypes.c_void_p(18), *ok[1:]) == -4                    # payload not 4-byte aligned
-    assert prep(*ok[:14], dummy, 16, None) == -7                       # workspace too small
+    assert prep(*ok[:14], dummy, 16, None, None) == -7                 # workspace too small
 
 
 def test_fused_rope_prepare_argument_errors_without_gpu():
@@ -80,7 +80,7 @@ def test_fused_rope_prepare_argument_errors_without_gpu():
 
     def call(*, cos=d, rotary=96, strides=st, ws_bytes=1 << 30, q=d):
         return h.xgb_sage_prepare_rope(q, strides, d, strides, d, strides, 1, 2, 300, 128, f, cos, d,
-                                       rotary, d, d, d, d, d, d, d, ws_bytes, None)
+                                       rotary, d, d, d, d, d, d, d, ws_bytes, None, None)
 
     assert call(q=None) == -1                                  # null input
     assert call(rotary=90) == -2                               # rotary/2 not a multiple of 8

@@ -62,12 +62,12 @@ SIGNATURES = {
     "xgb_sage_prepare_workspace": (c_i64, [c_i64, c_i64, c_i64]),
     "xgb_sage_prepare": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_int, c_i64, c_i64,
                                  c_i64, c_i64, c_float, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
-                                 c_i64, c_vp]),
+                                 c_i64, c_vp, c_vp]),
     "xgb_sage_prepare_rope": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_vp, c_i64p, c_i64, c_i64, c_i64,
                                       c_i64, c_float, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp,
-                                      c_vp, c_vp, c_i64, c_vp]),
+                                      c_vp, c_vp, c_i64, c_vp, c_vp]),
     "xgb_sage_prepare_wire": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_float, c_vp,
-                                      c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),
+                                      c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "xgb_attention_split_workspace_bytes": (c_i64, []),
     "xgb_sage_wire_stats_workspace": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
     "xgb_sage_wire_stats": (c_int, [c_vp, c_i64p, c_vp, c_i64p, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,

@@ -127,13 +127,13 @@ def sage_prepare(q, k, v, sm_scale: float | None = None, ws: SageWorkspace | Non
              i64_array(k.stride()), v.data_ptr(), i64_array(v.stride()), b, h, s, d, sm_scale,
              cos.data_ptr(), sin.data_ptr(), cos.shape[1], ws.q8.data_ptr(), ws.q_scale.data_ptr(),
              ws.k8.data_ptr(), ws.k_scale.data_ptr(), ws.v8.data_ptr(), ws.v_scale.data_ptr(),
-             ws.scratch.data_ptr(), ws.scratch_bytes, _stream(q))
+             ws.scratch.data_ptr(), ws.scratch_bytes, _err_flag(q.device).data_ptr(), _stream(q))
         return ws
     call("xgb_sage_prepare", q.data_ptr(), i64_array(q.stride()), k.data_ptr(),
          i64_array(k.stride()), v.data_ptr(), i64_array(v.stride()), dtype, b, h, s, d, sm_scale,
          ws.q8.data_ptr(), ws.q_scale.data_ptr(), ws.k8.data_ptr(), ws.k_scale.data_ptr(),
          ws.v8.data_ptr(), ws.v_scale.data_ptr(), ws.scratch.data_ptr(), ws.scratch_bytes,
-         _stream(q))
+         _err_flag(q.device).data_ptr(), _stream(q))
     return ws
 
 
@@ -155,7 +155,7 @@ def sage_prepare_wire(wire: torch.Tensor, *, peers: int, seq: int, batch: int, h
     call("xgb_sage_prepare_wire", wire.data_ptr(), peers, seq, batch, heads, valid_seq, peer_padding,
          sm_scale, ws.q8.data_ptr(), ws.q_scale.data_ptr(), ws.k8.data_ptr(), ws.k_scale.data_ptr(),
          ws.v8.data_ptr(), ws.v_scale.data_ptr(), ws.scratch.data_ptr(), ws.scratch_bytes,
-         torch.cuda.current_stream(wire.device).cuda_stream)
+         _err_flag(wire.device).data_ptr(), torch.cuda.current_stream(wire.device).cuda_stream)
     return ws
 
 

@@ -11,22 +11,23 @@
 // S_pad = roundup(S, 128); rows >= S are zero. Scales fp32: q/k
 // [B*H][S_pad/64], v [B*H][128].
 //
-// Two launches: per-chunk K sums and V abs-max (partials in the caller's
-// workspace; the last chunk of a head to finish turns them into the K mean
-// and the V scale), then the block quantiser. `xgb_sage_prepare_rope` also
-// applies the rotate-half RoPE of Q and K (x_base/x_base/operator/
+// One launch: a cooperative kernel of one or two CTAs per SM in three phases
+// split by grid barriers (bounded waits): (A) read Q, K and V once; quantise
+// Q and accumulate K column sums and V column abs-maxima; (B) per head, the K
+// mean and the V scale; (C) quantise K and V, walking the sequence backwards
+// so the rows phase A read last are still in L2. `xgb_sage_prepare_rope`
+// also applies the rotate-half RoPE of Q and K (x_base/x_base/operator/
 // h3_partial_rope.py:9-29) as it loads them, so the RoPE needs no pass of
 // its own.
 #include <cfloat>
 
+#include "sm100.cuh"
 #include "xgb_common.cuh"
 
 namespace xgb {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kStatsRows = 512;  // rows per stats CTA
-constexpr int kThreads = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <typename T>
@@ -39,32 +40,6 @@ __device__ __forceinline__ float tf<__half>(__half v) { return __half2float(v); 
 struct Strides {
   int64_t b, h, s;  // element strides; channel stride is 1
 };
-
-// Workspace: ksum partials [BH][chunks][128] fp32, vmax [BH][128] int,
-// done [BH] int (chunks of the head finished; zeroed with vmax per call),
-// kmean [BH][128] fp32.
-struct Workspace {
-  float* ksum;
-  int* vmax;
-  int* done;
-  float* kmean;
-  float* vscale;  // the caller's v_scale output
-};
-
-inline int64_t stats_chunks(int64_t seq) { return (seq + kStatsRows - 1) / kStatsRows; }
-
-inline Workspace carve(void* ws, int64_t bh, int64_t chunks) {
-  char* p = static_cast<char*>(ws);
-  Workspace w;
-  w.ksum = reinterpret_cast<float*>(p);
-  p += bh * chunks * kD * sizeof(float);
-  w.vmax = reinterpret_cast<int*>(p);
-  p += bh * kD * sizeof(int);
-  w.done = reinterpret_cast<int*>(p);
-  p += (bh + 3) / 4 * 4 * sizeof(int);
-  w.kmean = reinterpret_cast<float*>(p);
-  return w;
-}
 
 // Eight consecutive channels of one 16-byte load as fp32.
 template <typename T>
@@ -154,89 +129,6 @@ struct WireSource {
   }
 };
 
-// Per 512-row chunk of one head: channel sums of K and channel abs-max of V.
-// Thread t owns channels 8*(t%16)..+8 of rows t/16 + 16*i.
-// Grids of both kernels put (batch, head) fastest: consecutive CTAs read the
-// same sequence rows of all heads (contiguous in [B, S, H, D] storage and on
-// the wire, and sharing the RoPE table rows in L2).
-template <typename Src>
-__global__ void __launch_bounds__(kThreads) stats_kernel(Src src, int64_t heads, int64_t seq,
-                                                         Workspace w, int64_t chunks) {
-  const int64_t bh = blockIdx.x;
-  const int64_t chunk = blockIdx.y;
-  const int64_t b = bh / heads, h = bh % heads;
-  const int cg = threadIdx.x % 16;
-  const int rr = threadIdx.x / 16;
-  const int c0 = cg * 8;
-  const int64_t row_begin = chunk * kStatsRows;
-  const int64_t row_end = min(row_begin + kStatsRows, seq);
-  float sum[8], vmx[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    sum[j] = 0.f;
-    vmx[j] = 0.f;
-  }
-  for (int64_t r = row_begin + rr; r < row_end; r += kThreads / 16) {
-    float kx[8], vx[8];
-    Src::unpack(src.load(1, b, h, r, c0), kx);
-    Src::unpack(src.load(2, b, h, r, c0), vx);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      sum[j] += kx[j];
-      vmx[j] = fmaxf(vmx[j], fabsf(vx[j]));
-    }
-  }
-  __shared__ float part[kThreads / 16][kD];
-  __shared__ float vpart[kThreads / 16][kD];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    part[rr][c0 + j] = sum[j];
-    vpart[rr][c0 + j] = vmx[j];
-  }
-  __syncthreads();
-  if (threadIdx.x < kD) {
-    const int c = threadIdx.x;
-    float t = 0.f, m = 0.f;
-#pragma unroll
-    for (int i = 0; i < kThreads / 16; ++i) {
-      t += part[i][c];
-      m = fmaxf(m, vpart[i][c]);
-    }
-    w.ksum[(bh * chunks + chunk) * kD + c] = t;
-    atomicMax(&w.vmax[bh * kD + c], __float_as_int(m));
-  }
-  // The last chunk of the head to finish turns the partials into the K
-  // channel means and the V channel scales: eight slices each sum every
-  // eighth chunk, then the slices are added in a fixed order, so the result
-  // does not depend on which chunk finishes last.
-  __threadfence();
-  __syncthreads();
-  __shared__ int last;
-  if (threadIdx.x == 0) last = atomicAdd(&w.done[bh], 1) == chunks - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  constexpr int kSlices = 8;
-  float* slices = &part[0][0];  // reuse: kSlices x kD floats fit in part
-  static_assert(kSlices * kD <= (kThreads / 16) * kD, "slice scratch");
-  for (int k = threadIdx.x; k < kSlices * kD; k += kThreads) {
-    const int c = k % kD, slice = k / kD;
-    float sum = 0.f;
-    for (int64_t i = slice; i < chunks; i += kSlices) sum += __ldcg(&w.ksum[(bh * chunks + i) * kD + c]);
-    slices[slice * kD + c] = sum;
-  }
-  __syncthreads();
-  if (threadIdx.x < kD) {
-    const int c = threadIdx.x;
-    float t = 0.f;
-#pragma unroll
-    for (int j = 0; j < kSlices; ++j) t += slices[j * kD + c];
-    w.kmean[bh * kD + c] = __fdiv_rn(t, static_cast<float>(seq));
-    const float sc = __fdiv_rn(__int_as_float(__ldcg(&w.vmax[bh * kD + c])), 448.0f);
-    w.vscale[bh * kD + c] = fmaxf(sc, FLT_MIN);
-  }
-}
-
 // Block abs-max over the CTA (kN threads).
 template <int kN>
 __device__ __forceinline__ float block_absmax(float a, float* red) {
@@ -274,105 +166,6 @@ __device__ __forceinline__ void store_int8(int8_t* dst, int64_t row_stride, cons
   }
 }
 
-// One CTA of 512 threads per (64-row block, head); thread t owns channels
-// 8*(t%16)..+8 of rows t/16 + 32*i, i < 2 (16-byte loads of 8 channels).
-// All six loads of a thread (Q, K, V) are issued before any is used, kept as
-// raw 16-byte words, and Q, K and V are then quantised one after another.
-constexpr int kQuantThreads = 512;
-constexpr int kQuantRows = 64 * 16 / kQuantThreads;  // rows per thread
-
-template <typename Src>
-__global__ void __launch_bounds__(kQuantThreads, 2) quant_kernel(
-    Src src, int64_t heads, int64_t seq, int64_t s_pad, float q_mult, Workspace w,
-    const float* __restrict__ v_scale, int8_t* __restrict__ q8, float* __restrict__ q_scale,
-    int8_t* __restrict__ k8, float* __restrict__ k_scale, uint8_t* __restrict__ v8) {
-  const int64_t bh = blockIdx.x;
-  const int64_t b = bh / heads, h = bh % heads;
-  const int64_t blk = blockIdx.y;
-  const int cg = threadIdx.x % 16;
-  const int rr = threadIdx.x / 16;
-  const int c0 = cg * 8;
-  const int64_t row0 = blk * 64 + rr;
-  const int64_t off0 = (bh * s_pad + row0) * kD + c0;
-  constexpr int R = kQuantRows;
-  constexpr int kStep = 64 / R;
-  __shared__ float red[kQuantThreads / 32];
-  float x[R][8];
-  typename Src::Raw rq[R], rk[R], rv[R];
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    const int64_t row = row0 + kStep * i;
-    const bool ok = row < seq;
-    rq[i] = ok ? src.load(0, b, h, row, c0) : Src::zero();
-    rk[i] = ok ? src.load(1, b, h, row, c0) : Src::zero();
-    rv[i] = ok ? src.load(2, b, h, row, c0) : Src::zero();
-  }
-
-  // Values are recomputed from the raw words in each pass (the same
-  // operations give the same bits), which keeps few registers live.
-  bool ok[R];
-#pragma unroll
-  for (int i = 0; i < R; ++i) ok[i] = row0 + kStep * i < seq;
-
-  // Q: x * sm_scale * log2(e), per-block int8.
-  float a = 0.f;
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    Src::unpack(rq[i], x[i]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(__fmul_rn(x[i][j], q_mult)));
-  }
-  a = block_absmax<kQuantThreads>(a, red);
-  float sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
-  if (threadIdx.x == 0) q_scale[bh * (s_pad / 64) + blk] = sc;
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    Src::unpack(rq[i], x[i]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[i][j] = __fmul_rn(x[i][j], q_mult);  // rows >= seq: 0
-  }
-  store_int8(q8 + off0, kD, x, sc, __frcp_rn(sc));
-
-  // K: x - mean over the sequence, per-block int8.
-  float mean[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) mean[j] = w.kmean[bh * kD + c0 + j];
-  a = 0.f;
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    Src::unpack(rk[i], x[i]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a = fmaxf(a, ok[i] ? fabsf(__fsub_rn(x[i][j], mean[j])) : 0.f);
-  }
-  a = block_absmax<kQuantThreads>(a, red);
-  sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
-  if (threadIdx.x == 0) k_scale[bh * (s_pad / 64) + blk] = sc;
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    Src::unpack(rk[i], x[i]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[i][j] = ok[i] ? __fsub_rn(x[i][j], mean[j]) : 0.f;
-  }
-  store_int8(k8 + off0, kD, x, sc, __frcp_rn(sc));
-
-  // V: per-channel e4m3 (rows >= seq were loaded as zeros).
-  float vsc[8], vrc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    vsc[j] = v_scale[bh * kD + c0 + j];
-    vrc[j] = __frcp_rn(vsc[j]);
-  }
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    Src::unpack(rv[i], x[i]);
-    uint32_t q[4];
-#pragma unroll
-    for (int j = 0; j < 8; j += 2)
-      q[j / 2] = e4m3x2(div_by(x[i][j], vsc[j], vrc[j]), div_by(x[i][j + 1], vsc[j + 1], vrc[j + 1]));
-    *reinterpret_cast<uint2*>(v8 + off0 + kStep * i * kD) = make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
-  }
-}
-
 struct Outputs {
   int8_t* q8;
   float* q_scale;
@@ -382,30 +175,305 @@ struct Outputs {
   float* v_scale;
 };
 
-inline int64_t stats_workspace(int64_t bh, int64_t seq) {
-  return bh * stats_chunks(seq) * kD * 4 + bh * kD * 4 + (bh + 3) / 4 * 4 * 4 + bh * kD * 4;
+// The kernel: 512 threads per CTA; thread t owns channels 8*(t%16)..+8 of
+// rows t/16 and t/16 + 32 of a 64-row block (16-byte loads of 8 channels).
+constexpr int kPrepThreads = 512;
+constexpr int kPrepRows = 64 * 16 / kPrepThreads;  // rows per thread and block
+constexpr int kMaxPrepCtas = 296;                  // two per SM of a B200
+constexpr uint64_t kBarrierLimitNs = 2000000000ull;
+
+// Heads are taken in groups of G (the grid is P CTAs per head of a group):
+// CTA c works on head g0 + c % G of group g0 and on the blocks c / G,
+// c / G + P, ... of it.
+struct PrepShape {
+  int64_t heads, bh, seq, s_pad, n_blk;
+  int G, P;
+  float q_mult;
+};
+
+// Workspace: barrier counter (zeroed per call), then kmean [BH][128], then
+// the per-CTA partial K column sums and V column abs-maxima [BH][P][128].
+struct PrepWork {
+  int* arrive;
+  float* kmean;
+  float* part_k;
+  float* part_v;
+  int* err;
+};
+
+constexpr int64_t kCounterBytes = 64;
+
+// Partial rows per head: P <= kMaxPrepCtas / min(BH, kMaxPrepCtas), at least 1.
+inline int64_t partials_per_head(int64_t bh) {
+  return std::max<int64_t>(1, kMaxPrepCtas / std::min<int64_t>(bh, kMaxPrepCtas));
 }
 
-// Statistics, finalize and quantisation of [batch, heads, seq] rows read from `src`.
+inline int64_t prep_workspace(int64_t bh) {
+  return kCounterBytes + bh * kD * 4 + 2 * bh * partials_per_head(bh) * kD * 4;
+}
+
+inline PrepWork carve(void* ws, int64_t bh, int P, int* err) {
+  char* p = static_cast<char*>(ws);
+  PrepWork w;
+  w.arrive = reinterpret_cast<int*>(p);
+  p += kCounterBytes;
+  w.kmean = reinterpret_cast<float*>(p);
+  p += bh * kD * 4;
+  w.part_k = reinterpret_cast<float*>(p);
+  p += bh * P * kD * 4;
+  w.part_v = reinterpret_cast<float*>(p);
+  w.err = err;
+  return w;
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid-wide barrier of a cooperative launch: every CTA's writes before it are
+// visible to every CTA after it. The wait gives up after kBarrierLimitNs,
+// records a timeout in *err and returns false (every thread of the CTA).
+__device__ bool grid_barrier(int* arrive, int target, int* err, int* ok_smem) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = *ok_smem;
+    __threadfence();
+    atomicAdd(arrive, 1);
+    if (ok) {
+      const uint64_t t0 = sm100::global_timer_ns();
+      while (ld_acquire(arrive) < target) {
+        if (sm100::global_timer_ns() - t0 > kBarrierLimitNs) {
+          if (err) atomicExch(err, sm100::kErrTimeout);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+    *ok_smem = ok;
+  }
+  __syncthreads();
+  return *ok_smem != 0;
+}
+
 template <typename Src>
-int prepare(const Src& src, int64_t batch, int64_t heads, int64_t seq, float sm_scale,
-            const Outputs& o, void* workspace, cudaStream_t st) {
+__global__ void __launch_bounds__(kPrepThreads, 2) prepare_kernel(Src src, PrepShape sh, PrepWork w,
+                                                                  Outputs o) {
+  constexpr int R = kPrepRows;
+  constexpr int kStep = 64 / R;
+  const int cg = threadIdx.x % 16;
+  const int rr = threadIdx.x / 16;
+  const int c0 = cg * 8;
+  const int grid = static_cast<int>(gridDim.x);
+  const int hg = static_cast<int>(blockIdx.x) % sh.G;
+  const int pidx = static_cast<int>(blockIdx.x) / sh.G;
+  __shared__ float red[kPrepThreads / 32];
+  __shared__ float part[kPrepThreads / 16][kD];
+  __shared__ float vpart[kPrepThreads / 16][kD];
+  __shared__ int ok_smem;
+  if (threadIdx.x == 0) ok_smem = 1;
+  float x[R][8];
+
+  // ---- A: Q codes; K column sums and V column abs-maxima per CTA and head.
+  for (int64_t g0 = 0; g0 < sh.bh; g0 += sh.G) {
+    const int64_t bh = g0 + hg;
+    const bool active = bh < sh.bh;  // the last group may hold fewer heads (uniform per CTA)
+    const int64_t b = bh / sh.heads, h = bh % sh.heads;
+    float ksum[8], vmx[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      ksum[j] = 0.f;
+      vmx[j] = 0.f;
+    }
+    for (int64_t blk = pidx; active && blk < sh.n_blk; blk += sh.P) {
+      const int64_t row0 = blk * 64 + rr;
+      const int64_t off0 = (bh * sh.s_pad + row0) * kD + c0;
+      typename Src::Raw rq[R], rk[R], rv[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int64_t row = row0 + kStep * i;
+        const bool ok = row < sh.seq;
+        rq[i] = ok ? src.load(0, b, h, row, c0) : Src::zero();
+        rk[i] = ok ? src.load(1, b, h, row, c0) : Src::zero();
+        rv[i] = ok ? src.load(2, b, h, row, c0) : Src::zero();
+      }
+      // K and V statistics (rows >= seq were loaded as zeros).
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        float kx[8], vx[8];
+        Src::unpack(rk[i], kx);
+        Src::unpack(rv[i], vx);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          ksum[j] += kx[j];
+          vmx[j] = fmaxf(vmx[j], fabsf(vx[j]));
+        }
+      }
+      // Q: x * sm_scale * log2(e), per-block int8.
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        Src::unpack(rq[i], x[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[i][j] = __fmul_rn(x[i][j], sh.q_mult);  // rows >= seq: 0
+          a = fmaxf(a, fabsf(x[i][j]));
+        }
+      }
+      a = block_absmax<kPrepThreads>(a, red);
+      const float sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
+      if (threadIdx.x == 0) o.q_scale[bh * (sh.s_pad / 64) + blk] = sc;
+      store_int8(o.q8 + off0, kD, x, sc, __frcp_rn(sc));
+    }
+    if (active) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        part[rr][c0 + j] = ksum[j];
+        vpart[rr][c0 + j] = vmx[j];
+      }
+    }
+    __syncthreads();
+    if (active && threadIdx.x < kD) {
+      const int c = threadIdx.x;
+      float t = 0.f, m = 0.f;
+#pragma unroll 8
+      for (int i = 0; i < kPrepThreads / 16; ++i) {
+        t += part[i][c];
+        m = fmaxf(m, vpart[i][c]);
+      }
+      w.part_k[(bh * sh.P + pidx) * kD + c] = t;
+      w.part_v[(bh * sh.P + pidx) * kD + c] = m;
+    }
+    __syncthreads();
+  }
+  bool ok = grid_barrier(w.arrive, grid, w.err, &ok_smem);
+
+  // ---- B: per head, K mean = sum / seq and V scale = max(amax / 448, FLT_MIN),
+  // each from the head's P partial rows in a fixed order (four interleaved
+  // slices, added in slice order), so the result does not depend on timing.
+  for (int64_t bh = blockIdx.x; ok && bh < sh.bh; bh += grid) {
+    const int slice = threadIdx.x / kD, c = threadIdx.x % kD;
+    float t = 0.f, m = 0.f;
+    for (int p = slice; p < sh.P; p += kPrepThreads / kD) {
+      t += __ldcg(&w.part_k[(bh * sh.P + p) * kD + c]);
+      m = fmaxf(m, __ldcg(&w.part_v[(bh * sh.P + p) * kD + c]));
+    }
+    part[slice][c] = t;
+    vpart[slice][c] = m;
+    __syncthreads();
+    if (threadIdx.x < kD) {
+      float ts = 0.f, ms = 0.f;
+#pragma unroll
+      for (int s = 0; s < kPrepThreads / kD; ++s) {
+        ts += part[s][c];
+        ms = fmaxf(ms, vpart[s][c]);
+      }
+      w.kmean[bh * kD + c] = __fdiv_rn(ts, static_cast<float>(sh.seq));
+      o.v_scale[bh * kD + c] = fmaxf(__fdiv_rn(ms, 448.0f), FLT_MIN);
+    }
+    __syncthreads();
+  }
+  ok = grid_barrier(w.arrive, 2 * grid, w.err, &ok_smem) && ok;
+
+  // ---- C: K codes (mean-smoothed, per-block int8) and V codes (per-channel
+  // e4m3), groups and blocks in reverse order of phase A.
+  const int64_t n_groups = (sh.bh + sh.G - 1) / sh.G;
+  for (int64_t gi = n_groups - 1; ok && gi >= 0; --gi) {
+    const int64_t bh = gi * sh.G + hg;
+    if (bh >= sh.bh) continue;  // uniform per CTA
+    const int64_t b = bh / sh.heads, h = bh % sh.heads;
+    float mean[8], vsc[8], vrc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      mean[j] = __ldcg(&w.kmean[bh * kD + c0 + j]);
+      vsc[j] = __ldcg(&o.v_scale[bh * kD + c0 + j]);
+      vrc[j] = __frcp_rn(vsc[j]);
+    }
+    for (int64_t k = pidx; k < sh.n_blk; k += sh.P) {
+      const int64_t blk = sh.n_blk - 1 - k;
+      const int64_t row0 = blk * 64 + rr;
+      const int64_t off0 = (bh * sh.s_pad + row0) * kD + c0;
+      typename Src::Raw rk[R], rv[R];
+      bool valid[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int64_t row = row0 + kStep * i;
+        valid[i] = row < sh.seq;
+        rk[i] = valid[i] ? src.load(1, b, h, row, c0) : Src::zero();
+        rv[i] = valid[i] ? src.load(2, b, h, row, c0) : Src::zero();
+      }
+      // K: x - mean over the sequence, per-block int8 (rows >= seq: 0).
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        Src::unpack(rk[i], x[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[i][j] = valid[i] ? __fsub_rn(x[i][j], mean[j]) : 0.f;
+          a = fmaxf(a, fabsf(x[i][j]));
+        }
+      }
+      a = block_absmax<kPrepThreads>(a, red);
+      const float sc = a > 0.f ? __fdiv_rn(a, 127.0f) : 1.0f;
+      if (threadIdx.x == 0) o.k_scale[bh * (sh.s_pad / 64) + blk] = sc;
+      store_int8(o.k8 + off0, kD, x, sc, __frcp_rn(sc));
+      // V: per-channel e4m3 (rows >= seq were loaded as zeros).
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        Src::unpack(rv[i], x[i]);
+        uint32_t q[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2)
+          q[j / 2] = e4m3x2(div_by(x[i][j], vsc[j], vrc[j]), div_by(x[i][j + 1], vsc[j + 1], vrc[j + 1]));
+        *reinterpret_cast<uint2*>(o.v8 + off0 + kStep * i * kD) = make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
+      }
+    }
+  }
+}
+
+// Cooperative launch of prepare_kernel over [BH, seq] rows read from `src`.
+template <typename Src>
+int prepare(const Src& src, int64_t batch, int64_t heads, int64_t seq, float sm_scale, const Outputs& o, void* workspace,
+            int64_t workspace_bytes, int* err, cudaStream_t st) {
+  if (!workspace || workspace_bytes < prep_workspace(batch * heads)) return XGB_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 15u) return XGB_ERR_ALIGN;
+  static int occupancy[64] = {};  // per device; the kernel's static shape fixes it
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return XGB_ERR_DEVICE;
+  if (occupancy[dev] == 0) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, prepare_kernel<Src>, kPrepThreads, 0) !=
+        cudaSuccess)
+      return XGB_ERR_LAUNCH;
+    occupancy[dev] = occ;
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return XGB_ERR_DEVICE;
+  const int64_t cap = std::min<int64_t>(kMaxPrepCtas, static_cast<int64_t>(occupancy[dev]) * sms);
+  if (cap <= 0) return XGB_ERR_LAUNCH;
   const int64_t bh = batch * heads;
-  const int64_t chunks = stats_chunks(seq);
-  const int64_t s_pad = (seq + 127) / 128 * 128;
-  Workspace w = carve(workspace, bh, chunks);
-  w.vscale = o.v_scale;
-  // vmax and the per-head chunk counters, contiguous
-  const size_t zero_bytes = bh * kD * sizeof(int) + (bh + 3) / 4 * 4 * sizeof(int);
-  if (cudaMemsetAsync(w.vmax, 0, zero_bytes, st) != cudaSuccess) return XGB_ERR_LAUNCH;
-  const float q_mult = sm_scale * kLog2e;
-  if (chunks > 65535 || s_pad / 64 > 65535) return XGB_ERR_SHAPE;  // grid y
-  const dim3 sgrid(static_cast<unsigned>(bh), static_cast<unsigned>(chunks));
-  const dim3 qgrid(static_cast<unsigned>(bh), static_cast<unsigned>(s_pad / 64));
-  stats_kernel<<<sgrid, kThreads, 0, st>>>(src, heads, seq, w, chunks);
-  quant_kernel<<<qgrid, kQuantThreads, 0, st>>>(src, heads, seq, s_pad, q_mult, w, o.v_scale, o.q8,
-                                                o.q_scale, o.k8, o.k_scale, o.v8);
-  return launch_status();
+  PrepShape sh;
+  sh.heads = heads;
+  sh.bh = bh;
+  sh.seq = seq;
+  sh.s_pad = (seq + 127) / 128 * 128;
+  sh.n_blk = sh.s_pad / 64;
+  sh.G = static_cast<int>(std::min<int64_t>(bh, cap));
+  sh.P = static_cast<int>(cap / sh.G);
+  sh.q_mult = sm_scale * kLog2e;
+  PrepWork w = carve(workspace, bh, sh.P, err);
+  if (cudaMemsetAsync(w.arrive, 0, sizeof(int), st) != cudaSuccess) return XGB_ERR_LAUNCH;
+  Src s = src;
+  Outputs out = o;
+  void* args[] = {&s, &sh, &w, &out};
+  const unsigned grid = static_cast<unsigned>(sh.G) * static_cast<unsigned>(sh.P);
+  if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&prepare_kernel<Src>), dim3(grid),
+                                  dim3(kPrepThreads), args, 0, st) != cudaSuccess)
+    return XGB_ERR_LAUNCH;
+  return XGB_OK;
 }
 
 }  // namespace
@@ -415,7 +483,7 @@ using namespace xgb;
 
 XGB_API int64_t xgb_sage_prepare_workspace(int64_t batch, int64_t heads, int64_t seq) {
   if (batch <= 0 || heads <= 0 || seq <= 0) return 0;
-  return stats_workspace(batch * heads, seq);
+  return prep_workspace(batch * heads);
 }
 
 XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void* k,
@@ -423,7 +491,8 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
                              int dtype, int64_t batch, int64_t heads, int64_t seq,
                              int64_t head_dim, float sm_scale, int8_t* q8, float* q_scale,
                              int8_t* k8, float* k_scale, uint8_t* v8, float* v_scale,
-                             void* workspace, int64_t workspace_bytes, void* stream) {
+                             void* workspace, int64_t workspace_bytes, int* error_flag,
+                             void* stream) {
   if (!q || !k || !v || !q_strides || !k_strides || !v_strides) return XGB_ERR_ARG;
   if (!q8 || !q_scale || !k8 || !k_scale || !v8 || !v_scale) return XGB_ERR_ARG;
   if (dtype != XGB_BF16 && dtype != XGB_F16) return XGB_ERR_ARG;
@@ -440,8 +509,6 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
   if ((reinterpret_cast<uintptr_t>(q8) | reinterpret_cast<uintptr_t>(k8) |
        reinterpret_cast<uintptr_t>(v8)) & 15u)
     return XGB_ERR_ALIGN;
-  const int64_t need = xgb_sage_prepare_workspace(batch, heads, seq);
-  if (!workspace || workspace_bytes < need) return XGB_ERR_WORKSPACE;
   const Strides qs{q_strides[0], q_strides[1], q_strides[2]};
   const Strides ks{k_strides[0], k_strides[1], k_strides[2]};
   const Strides vs{v_strides[0], v_strides[1], v_strides[2]};
@@ -450,12 +517,14 @@ XGB_API int xgb_sage_prepare(const void* q, const int64_t* q_strides, const void
     using S = StridedSource<__nv_bfloat16>;
     const S src{{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                  static_cast<const __nv_bfloat16*>(v)}, {qs, ks, vs}};
-    return prepare(src, batch, heads, seq, sm_scale, o, workspace, as_stream(stream));
+    return prepare(src, batch, heads, seq, sm_scale, o, workspace, workspace_bytes, error_flag,
+                 as_stream(stream));
   }
   using S = StridedSource<__half>;
   const S src{{static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v)},
               {qs, ks, vs}};
-  return prepare(src, batch, heads, seq, sm_scale, o, workspace, as_stream(stream));
+  return prepare(src, batch, heads, seq, sm_scale, o, workspace, workspace_bytes, error_flag,
+                 as_stream(stream));
 }
 
 XGB_API int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const void* k,
@@ -464,7 +533,7 @@ XGB_API int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const
                                   float sm_scale, const float* cos, const float* sin, int64_t rotary,
                                   int8_t* q8, float* q_scale, int8_t* k8, float* k_scale, uint8_t* v8,
                                   float* v_scale, void* workspace, int64_t workspace_bytes,
-                                  void* stream) {
+                                  int* error_flag, void* stream) {
   if (!q || !k || !v || !q_strides || !k_strides || !v_strides || !cos || !sin) return XGB_ERR_ARG;
   if (!q8 || !q_scale || !k8 || !k_scale || !v8 || !v_scale) return XGB_ERR_ARG;
   if (head_dim != kD) return XGB_ERR_SHAPE;
@@ -481,8 +550,6 @@ XGB_API int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const
   if ((reinterpret_cast<uintptr_t>(q8) | reinterpret_cast<uintptr_t>(k8) |
        reinterpret_cast<uintptr_t>(v8)) & 15u)
     return XGB_ERR_ALIGN;
-  const int64_t need = xgb_sage_prepare_workspace(batch, heads, seq);
-  if (!workspace || workspace_bytes < need) return XGB_ERR_WORKSPACE;
   using B = StridedSource<__nv_bfloat16>;
   RopeSource src{};
   src.base = B{{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
@@ -494,14 +561,16 @@ XGB_API int xgb_sage_prepare_rope(const void* q, const int64_t* q_strides, const
   src.sin = sin;
   src.rotary = static_cast<int>(rotary);
   const Outputs o{q8, q_scale, k8, k_scale, v8, v_scale};
-  return prepare(src, batch, heads, seq, sm_scale, o, workspace, as_stream(stream));
+  return prepare(src, batch, heads, seq, sm_scale, o, workspace, workspace_bytes, error_flag,
+                 as_stream(stream));
 }
 
 XGB_API int xgb_sage_prepare_wire(const uint8_t* payload, int64_t peers, int64_t seq,
                                   int64_t batch, int64_t heads, int64_t valid_seq,
                                   int64_t peer_padding, float sm_scale, int8_t* q8, float* q_scale,
                                   int8_t* k8, float* k_scale, uint8_t* v8, float* v_scale,
-                                  void* workspace, int64_t workspace_bytes, void* stream) {
+                                  void* workspace, int64_t workspace_bytes, int* error_flag,
+                                  void* stream) {
   if (!payload || !q8 || !q_scale || !k8 || !k_scale || !v8 || !v_scale) return XGB_ERR_ARG;
   if (peers <= 0 || seq <= 0 || batch <= 0 || heads <= 0) return XGB_ERR_SHAPE;
   if (valid_seq <= 0 || valid_seq > peers * seq || peers * seq > INT32_MAX) return XGB_ERR_SHAPE;
@@ -512,8 +581,6 @@ XGB_API int xgb_sage_prepare_wire(const uint8_t* payload, int64_t peers, int64_t
       ((reinterpret_cast<uintptr_t>(q8) | reinterpret_cast<uintptr_t>(k8) |
         reinterpret_cast<uintptr_t>(v8)) & 15u))
     return XGB_ERR_ALIGN;
-  const int64_t need = xgb_sage_prepare_workspace(batch, heads, valid_seq);
-  if (!workspace || workspace_bytes < need) return XGB_ERR_WORKSPACE;
   WireSource src{};
   src.payload = payload;
   src.batch = batch;
@@ -522,5 +589,6 @@ XGB_API int xgb_sage_prepare_wire(const uint8_t* payload, int64_t peers, int64_t
   src.peer_bytes = 3 * src.peer_rows * (kD + 4) + peer_padding;
   src.div_seq = make_fastdiv(static_cast<uint32_t>(seq));
   const Outputs o{q8, q_scale, k8, k_scale, v8, v_scale};
-  return prepare(src, batch, heads, valid_seq, sm_scale, o, workspace, as_stream(stream));
+  return prepare(src, batch, heads, valid_seq, sm_scale, o, workspace, workspace_bytes, error_flag,
+                 as_stream(stream));
 }
