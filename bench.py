@@ -1002,19 +1002,19 @@ def c5_timing(args, world, rank, dev, group, comm_stream, barrier, max_over_rank
 
 def kernels_per_step(precision, world, phaa, wire="fp8"):
     """Our kernel launches per layer.
-    SP = 1: Sage: statistics + quantisation (RoPE fused in) + attention; BF16:
-    RoPE + attention.
+    SP = 1: Sage: the preparation (one cooperative launch, RoPE fused in) +
+    attention; BF16: RoPE + attention.
     SP > 1, Sage over the FP8 wire, per PHAA chunk: QKV encode (RoPE fused),
-    statistics + quantisation read from the received wire, attention, return
-    encode, return decode. BF16: RoPE, then per chunk the attention (the
-    Ulysses exchange is NCCL's). INT8 wire (one chunk): statistics, statistics
+    the preparation read from the received wire, attention, return encode,
+    return decode. BF16: RoPE, then per chunk the attention (the Ulysses
+    exchange is NCCL's). INT8 wire (one chunk): statistics, statistics
     finalize, encode, attention, return encode, decode."""
     if world == 1:
-        return 3 if precision == "sage" else 2
+        return 2
     if precision == "sage" and wire == "int8":
         return 6
     if precision == "sage":
-        return 6 * phaa
+        return 5 * phaa
     return 1 + phaa
 
 

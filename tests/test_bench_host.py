@@ -77,9 +77,9 @@ def test_return_wire_is_per_row(small):
 
 
 def test_launch_accounting():
-    assert bench.kernels_per_step("sage", 1, 1) == 3
+    assert bench.kernels_per_step("sage", 1, 1) == 2
     assert bench.kernels_per_step("bf16", 1, 1) == 2
-    assert bench.kernels_per_step("sage", 8, 1) == 6
-    assert bench.kernels_per_step("sage", 8, 3) == 18
+    assert bench.kernels_per_step("sage", 8, 1) == 5
+    assert bench.kernels_per_step("sage", 8, 3) == 15
     assert bench.kernels_per_step("sage", 2, 1, "int8") == 6
     assert bench.kernels_per_step("bf16", 4, 2) == 3
