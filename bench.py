@@ -839,7 +839,13 @@ def main():
                                 "the head-sharded attention output before the return exchange")
             returned = _wire_round_trip(pre_got.view(-1, HEAD_DIM)).view(PARITY_ROWS, WIDTH)
             same = (returned == parity_got)
-            parity["post_return_wire"] = {k2: parity.pop(k2) for k2 in ("cosine_min", "cosine_mean", "max_abs", "bar", "ok")}
+            post = {k2: parity.pop(k2) for k2 in ("cosine_min", "cosine_mean", "max_abs")}
+            for k2 in ("bar", "ok"):
+                parity.pop(k2)
+            post["note"] = ("reported, not gated: the return wire rounds each output row to e4m3 on its own, "
+                            "so two outputs that differ by the Sage noise straddle different codes; "
+                            "the bar applies before the return wire, and the return path is checked bit for bit")
+            parity["post_return_wire"] = post
             parity["pre_return_wire"] = pre
             parity["return_path_exact"] = {
                 "elements": int(same.numel()), "equal": int(same.sum()),
