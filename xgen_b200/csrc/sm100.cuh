@@ -390,22 +390,19 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Packed fp32x2 FMA / add (one instruction for two lanes of work).
+// Packed fp32x2 FMA / add (one instruction for two lanes of work; each lane
+// rounds as the scalar fmaf / fadd does).
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
                                       float c0, float c1) {
-  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
-      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
-      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+  const float2 d = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(c0, c1));
+  d0 = d.x;
+  d1 = d.y;
 }
 
 __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 a, b, d;\n\t"
-      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
-      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  const float2 d = __fadd2_rn(make_float2(a0, a1), make_float2(b0, b1));
+  d0 = d.x;
+  d1 = d.y;
 }
 
 // 2^x for two values on the FMA/ALU pipes, in packed fp32x2 arithmetic:
