@@ -90,6 +90,7 @@ constexpr uint32_t kInitBWord = 0x5C5C5C5Cu;  // e5m2 256 in every byte
 constexpr int kTurnBar = 1;  // named barriers 1, 2: exp turn of WG0, WG1
 constexpr int kEpiBar = 3;   // named barrier 3: the 256 softmax threads in the split epilogue
 constexpr uint32_t kMagic = 0x4B400000u;
+constexpr int kRevTiles = 148;  // Q-tile pairs per key-order group (BF16)
 
 template <bool kSage>
 struct Cfg {
@@ -223,6 +224,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int per = split ? (n_all + p.splits - 1) / p.splits : n_all;
   const int kv0 = split ? ((cta - p.n_full) % p.splits) * per : 0;
   const int n_kv = split ? min(per, n_all - kv0) : n_all;
+  // BF16: consecutive groups of kRevTiles Q-tile pairs of a head (about one
+  // wave of CTAs) walk the keys in opposite directions, so each group starts
+  // on the K/V tiles the previous one read last, still in L2 (one head's bf16
+  // K/V is about half the L2). Depends only on the item, so a result never
+  // depends on how many heads a launch holds. Sage keeps the forward order:
+  // its K/V stay in L2 anyway, and its P quantisation follows the key order.
+  const bool rev = !kSage && (((item % p.n_qt) / kRevTiles) & 1);
+  auto kv_at = [&](int t) { return kv0 + (rev ? n_kv - 1 - t : t); };
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -276,10 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t >= C::kStages) ok = mbar_wait(&bars->kv_empty[s], ((t / C::kStages) - 1) & 1, p.err);
         if (!ok) break;
         mbar_arrive_expect_tx(&bars->k_full[s], C::kKVBytes);
-        load_rows<kSage, kWire>(&k_map, smem + C::kKOff + s * C::kKVBytes, &bars->k_full[s], (kv0 + t) * kBN,
+        load_rows<kSage, kWire>(&k_map, smem + C::kKOff + s * C::kKVBytes, &bars->k_full[s], kv_at(t) * kBN,
                          bh, p.heads, C::kSub);
         mbar_arrive_expect_tx(&bars->v_full[s], C::kKVBytes);
-        load_rows<kSage, kWire>(&v_map, smem + C::kVOff + s * C::kKVBytes, &bars->v_full[s], (kv0 + t) * kBN,
+        load_rows<kSage, kWire>(&v_map, smem + C::kVOff + s * C::kKVBytes, &bars->v_full[s], kv_at(t) * kBN,
                          bh, p.heads, C::kSub);
         issued = t + 1;
       }
@@ -405,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The map is monotone, so the max runs on floats and no conversion
       // instruction is needed. Padding keys (>= valid, last tile only) get a
       // sentinel far below any real score.
-      const int valid = p.seq_kv - (kv0 + t) * kBN;
+      const int valid = p.seq_kv - kv_at(t) * kBN;
       const float comb = kSage ? qs * ks : p.scale_log2;
       float comb4[4];
       if constexpr (kSage && kWire) {
