@@ -63,6 +63,10 @@ def parse():
                          "so the exchanges of overlapped PHAA chunks take few SMs from the attention")
     ap.add_argument("--wire", choices=("fp8", "int8"), default="fp8",
                     help="SP gather transport (Sage): the FP8 wire, or Sage-quantised INT8")
+    ap.add_argument("--wire-transport", choices=("peer", "nccl"), default="peer",
+                    help="how the FP8-wire Q/K/V gather crosses GPUs (Sage, SP > 1): one kernel that "
+                         "encodes straight into the peers' receive buffers over NVLink (peer), or the "
+                         "encode followed by NCCL all_to_all_single (nccl)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-block", action="store_true", help="skip the full DiT block timing")
@@ -689,6 +693,7 @@ def main():
     rank, world, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    os.environ["XGB_SP_PEER_WIRE"] = "1" if args.wire_transport == "peer" else "0"
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     group = None
@@ -862,7 +867,7 @@ def main():
     barrier()
 
     kernels_per_layer = kernels_per_step(args.precision, world, min(args.phaa_num, HEADS // world),
-                                         args.wire)
+                                         args.wire, args.wire_transport)
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -874,6 +879,8 @@ def main():
         "clocks": clocks.summary(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
         "block": block, "c5": c5, "parity": parity,
     }
+    if world > 1 and args.precision == "sage" and args.wire == "fp8":
+        line["sp_transport"] = args.wire_transport
     if rank == 0:
         print(json.dumps(line), flush=True)
     del out
@@ -1006,13 +1013,16 @@ def c5_timing(args, world, rank, dev, group, comm_stream, barrier, max_over_rank
             "adaln": "a fresh random [3, 6*3072] table per step"}
 
 
-def kernels_per_step(precision, world, phaa, wire="fp8"):
+def kernels_per_step(precision, world, phaa, wire="fp8", transport="nccl"):
     """Our kernel launches per layer.
     SP = 1: Sage: the preparation (one cooperative launch, RoPE fused in) +
     attention; BF16: RoPE + attention.
     SP > 1, Sage over the FP8 wire, per PHAA chunk: QKV encode (RoPE fused),
     the preparation read from the received wire, attention, return encode,
-    return decode. BF16: RoPE, then per chunk the attention (the Ulysses
+    return decode; over peer memory the encode writes the peers' buffers and
+    four flag kernels order it (wait for the slot to be freed, signal
+    arrival, wait for the peers' arrivals, signal freed after the
+    preparation). BF16: RoPE, then per chunk the attention (the Ulysses
     exchange is NCCL's). INT8 wire (one chunk): statistics, statistics
     finalize, encode, attention, return encode, decode."""
     if world == 1:
@@ -1020,7 +1030,7 @@ def kernels_per_step(precision, world, phaa, wire="fp8"):
     if precision == "sage" and wire == "int8":
         return 6
     if precision == "sage":
-        return 5 * phaa
+        return (9 if transport == "peer" else 5) * phaa
     return 1 + phaa
 
 

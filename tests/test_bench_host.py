@@ -81,5 +81,7 @@ def test_launch_accounting():
     assert bench.kernels_per_step("bf16", 1, 1) == 2
     assert bench.kernels_per_step("sage", 8, 1) == 5
     assert bench.kernels_per_step("sage", 8, 3) == 15
+    assert bench.kernels_per_step("sage", 8, 1, "fp8", "peer") == 9
+    assert bench.kernels_per_step("sage", 1, 1, "fp8", "peer") == 2
     assert bench.kernels_per_step("sage", 2, 1, "int8") == 6
     assert bench.kernels_per_step("bf16", 4, 2) == 3

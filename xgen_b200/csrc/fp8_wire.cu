@@ -299,6 +299,123 @@ __global__ void __launch_bounds__(kThreads) wire_encode_bf16_kernel(EncodeArgs a
   }
 }
 
+// Peer form of wire_encode_bf16_kernel<2> (bf16 Q/K/V, 128 channels, the
+// same bytes): the encoded rows go straight into each destination rank's
+// receive buffer over NVLink instead of a local send buffer that an
+// all-to-all then moves. dst[p] is where this rank's section starts in peer
+// p's receive buffer (the offset an all_to_all_single would deliver it to).
+// A warp owns 4 consecutive (seq, batch) positions of one peer; their rows
+// for all heads are one contiguous span of the section, 16-byte aligned when
+// a peer holds a multiple of 4 positions. The warp encodes the span into
+// shared memory and then writes it out with 16-byte stores, so the link
+// carries full sectors rather than the 4-byte pieces the row encoder makes.
+constexpr int kMaxPeers = 8;
+constexpr int kPeerPositions = 4;  // per warp: 8 lanes x 16 channels per position
+
+struct PeerDst {
+  uint8_t* dst[kMaxPeers];
+};
+
+__global__ void __launch_bounds__(kThreads) wire_encode_peers_kernel(EncodeArgs a, PeerDst pd) {
+  extern __shared__ __align__(16) uint8_t stage[];
+  constexpr int V = 2;
+  constexpr int G = 8;
+  constexpr int64_t kRowBytes = 132;
+  const int slot = blockIdx.y;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & (G - 1);
+  const int heads = static_cast<int>(a.heads);
+  const int64_t span = kPeerPositions * heads * kRowBytes;
+  uint8_t* st = stage + warp * span;
+  const int64_t positions = a.rows / a.heads;
+  const int64_t pos0 = (static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + warp) * kPeerPositions;
+  if (pos0 >= positions) return;  // whole warps: positions % 4 == 0
+  const int local = lane / G;
+  const uint32_t pr = static_cast<uint32_t>(pos0 + local);
+  const uint32_t q2 = fast_div(pr, a.div_batch);  // peer * seq + s
+  const uint32_t bat = pr - q2 * a.div_batch.d;
+  const uint32_t peer = fast_div(q2, a.div_seq);
+  const uint32_t s = q2 - peer * a.div_seq.d;
+  const int c0 = sub * 8 * V;
+  const bool has = static_cast<int64_t>(peer) * a.seq + s < a.valid_seq;
+  const bool rope = has && slot < 2 && c0 < a.rotary;
+  const int half = static_cast<int>(a.rotary / 2);
+  const bool first = c0 < half;
+  uint32_t cw[V][4], sw[V][4];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    if (rope) {
+      load_cos_sin8(a.cos + static_cast<int64_t>(s) * a.rotary + c0 + 8 * v,
+                    a.sin + static_cast<int64_t>(s) * a.rotary + c0 + 8 * v, cw[v], sw[v]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cw[v][k] = sw[v][k] = 0;
+    }
+  }
+  const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(a.src[slot]) + peer * a.st[slot][0] +
+                              s * a.st[slot][1] + bat * a.st[slot][2] + c0;
+  const int plane = (lane & ~(G - 1)) | (c0 >= a.rotary ? sub : (first ? sub + half / (8 * V) : sub - half / (8 * V)));
+  const int64_t hstride = a.st[slot][3];
+  constexpr float kRcp448 = 1.0f / 448.0f;  // RN(1/448)
+  uint8_t* row0 = st + local * heads * kRowBytes;
+  for (int h0 = 0; h0 < heads; h0 += kHeadBlock) {
+    uint4 raw[kHeadBlock][V];
+#pragma unroll
+    for (int j = 0; j < kHeadBlock; ++j) {
+      const bool hj = has && h0 + j < heads;
+      const __nv_bfloat16* src = base + (h0 + j) * hstride;
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        raw[j][v] = hj ? __ldg(reinterpret_cast<const uint4*>(src) + v) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < kHeadBlock; ++j) {
+      if (h0 + j >= heads) break;  // uniform across the warp
+      float x[V][8];
+      float m = 0.f;
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        if (slot < 2 && a.rotary > 0) {  // uniform: every lane of the group shuffles
+          uint4 par;
+          par.x = __shfl_sync(0xffffffffu, raw[j][v].x, plane);
+          par.y = __shfl_sync(0xffffffffu, raw[j][v].y, plane);
+          par.z = __shfl_sync(0xffffffffu, raw[j][v].z, plane);
+          par.w = __shfl_sync(0xffffffffu, raw[j][v].w, plane);
+          if (rope) raw[j][v] = rope8_bf16(raw[j][v], par, first, cw[v], sw[v]);
+        }
+        unpack_bf16x8(raw[j][v], x[v]);
+        m = fmaxf(fmaxf(m, fabsf(x[v][0])), fabsf(x[v][1]));
+        m = fmaxf(fmaxf(m, fabsf(x[v][2])), fabsf(x[v][3]));
+        m = fmaxf(fmaxf(m, fabsf(x[v][4])), fabsf(x[v][5]));
+        m = fmaxf(fmaxf(m, fabsf(x[v][6])), fabsf(x[v][7]));
+      }
+      for (int o = G / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float scale = fmaxf(div_by(m, 448.0f, kRcp448), 1.0e-12f);
+      uint8_t* row = row0 + (h0 + j) * kRowBytes;
+      const float y = __frcp_rn(scale);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const uint32_t e0 = e4m3x2(div_by(x[v][0], scale, y), div_by(x[v][1], scale, y));
+        const uint32_t e1 = e4m3x2(div_by(x[v][2], scale, y), div_by(x[v][3], scale, y));
+        const uint32_t e2 = e4m3x2(div_by(x[v][4], scale, y), div_by(x[v][5], scale, y));
+        const uint32_t e3 = e4m3x2(div_by(x[v][6], scale, y), div_by(x[v][7], scale, y));
+        reinterpret_cast<uint32_t*>(row + c0 + 8 * v)[0] = e0 | (e1 << 16);
+        reinterpret_cast<uint32_t*>(row + c0 + 8 * v)[1] = e2 | (e3 << 16);
+      }
+      if (sub == 0) *reinterpret_cast<float*>(row + 128) = scale;
+    }
+  }
+  __syncwarp();
+  // The span's place in the destination section: [slot][seq, batch, head] rows.
+  const uint32_t dpeer = __shfl_sync(0xffffffffu, peer, 0);
+  const int64_t pos_in_peer = pos0 - static_cast<int64_t>(dpeer) * a.seq * a.batch;
+  uint4* out = reinterpret_cast<uint4*>(pd.dst[dpeer] + (slot * a.peer_rows + pos_in_peer * heads) * kRowBytes);
+  const uint4* in = reinterpret_cast<const uint4*>(st);
+  for (int64_t i = lane; i < span / 16; i += 32) out[i] = in[i];
+  __threadfence_system();  // these stores before anything this thread's stream does next
+}
+
 struct DecodeArgs {
   const uint8_t* payload;
   void* dst[kMaxStreams];
@@ -494,4 +611,53 @@ XGB_API int xgb_fp8_wire_decode(const uint8_t* payload, void* const* dests, int 
   }
   return xgb_fp8_wire_decode_view(payload, dests, strides, streams, peers, peer_rows, 1, 1, width,
                                   rows, peer_padding, dtype, stream);
+}
+
+XGB_API int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t* strides, int64_t peers,
+                                      int64_t seq, int64_t batch, int64_t heads, const float* cos,
+                                      const float* sin, int64_t rotary, int64_t valid_seq,
+                                      uint8_t* const* peer_dst, void* stream) {
+  if (!sources || !strides || !peer_dst) return XGB_ERR_ARG;
+  if (peers <= 0 || peers > kMaxPeers || seq <= 0 || batch <= 0 || heads <= 0) return XGB_ERR_SHAPE;
+  if (valid_seq <= 0 || valid_seq > peers * seq) return XGB_ERR_SHAPE;
+  // whole warps of 4 positions inside one peer; shared-memory span per warp
+  if ((seq * batch) % kPeerPositions || heads > 12) return XGB_ERR_SHAPE;
+  if (rotary < 0 || rotary % 32 || rotary > 128) return XGB_ERR_SHAPE;
+  if (rotary > 0 && (!cos || !sin)) return XGB_ERR_ARG;
+  if (rotary > 0 && ((reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) & 15u))
+    return XGB_ERR_ALIGN;
+  EncodeArgs a{};
+  a.rows = peers * seq * batch * heads;
+  if (a.rows > INT32_MAX) return XGB_ERR_SHAPE;
+  for (int s = 0; s < 3; ++s) {
+    if (!sources[s]) return XGB_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(sources[s]) & 15u) return XGB_ERR_ALIGN;
+    a.src[s] = sources[s];
+    for (int d = 0; d < 4; ++d) {
+      a.st[s][d] = strides[4 * s + d];
+      if (a.st[s][d] % 8) return XGB_ERR_STRIDE;
+    }
+  }
+  PeerDst pd{};
+  for (int p = 0; p < peers; ++p) {
+    if (!peer_dst[p]) return XGB_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(peer_dst[p]) & 15u) return XGB_ERR_ALIGN;
+    pd.dst[p] = peer_dst[p];
+  }
+  a.peers = peers; a.seq = seq; a.batch = batch; a.heads = heads; a.width = 128;
+  a.peer_rows = a.rows / peers;
+  a.peer_padding = 0; a.streams = 3; a.valid_seq = valid_seq;
+  a.div_heads = make_fastdiv(static_cast<uint32_t>(heads));
+  a.div_batch = make_fastdiv(static_cast<uint32_t>(batch));
+  a.div_seq = make_fastdiv(static_cast<uint32_t>(seq));
+  a.cos = cos; a.sin = sin; a.rotary = rotary; a.payload = nullptr;
+  const int smem = (kThreads / 32) * kPeerPositions * static_cast<int>(heads) * 132;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(wire_encode_peers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess)
+    return XGB_ERR_LAUNCH;
+  const int64_t positions = a.rows / heads;
+  const dim3 grid(static_cast<unsigned>(cdiv(positions, (kThreads / 32) * kPeerPositions)), 3);
+  wire_encode_peers_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(a, pd);
+  return launch_status();
 }

@@ -33,6 +33,7 @@ import torch.distributed as dist
 
 from ..sp.padding import get_pad_manager
 from . import fp8_transport as fp8
+from . import peer_wire
 
 
 class _HostStreams:
@@ -171,9 +172,13 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             for t in chunks[i]:
                 t.record_stream(comm_stream)
             return
-        if from_wire:
+        if from_wire and peer_wire.enabled() and peer_wire.eligible(chunks[i], D, sp_group):
+            # B200: encode straight into the peers' receive buffers (no NCCL step)
+            wires[i] = peer_wire.exchange_wire(chunks[i], D, sp_group,
+                                               rotary_emb=rotary_emb if fuse_rope else None)
+        elif from_wire:
             wires[i] = fp8.fp8_exchange_wire(chunks[i], D, sp_group,
-                                             rotary_emb=rotary_emb if fuse_rope else None)
+                                             rotary_emb=rotary_emb if fuse_rope else None) + (None,)
         elif fp8_transport:
             fp8.fp8_all_to_all_many(gather[i], chunks[i], D, sp_group,
                                     rotary_emb=rotary_emb if fuse_rope else None)
@@ -196,7 +201,7 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             acc.current_stream().wait_event(gathered[step])
         cs = sizes[step]
         if from_wire:
-            wire, peers, peer_padding = wires[step]
+            wire, peers, peer_padding, ticket = wires[step]
             wires[step] = None
             send = torch.empty((W_S, Sq, B, cs, D), device=query.device, dtype=query.dtype)
             if pad > 0:
@@ -205,7 +210,10 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
             attention_fn.attend_fp8_wire(wire, peers=peers, seq=Sq, batch=B, heads=cs,
                                          valid_seq=W_S * Sq - pad, peer_padding=peer_padding,
                                          out=view.narrow(2, 0, W_S * Sq - pad))
-            wire.record_stream(acc.current_stream())  # allocated on the comm stream
+            if ticket is None:
+                wire.record_stream(acc.current_stream())  # allocated on the comm stream
+            else:
+                peer_wire.release(ticket)  # the Sage preparation has read it
             results[step] = send.flatten(-2, -1)
         else:
             if direct_gather:
