@@ -78,6 +78,9 @@ def parse():
     ap.add_argument("--linear-only", action="store_true",
                     help="time the FP8 Linear stack of one block (BASELINE config 4)")
     ap.add_argument("--sp", type=int, default=8, help="SP degree that sets the linear-stack M")
+    ap.add_argument("--sp-exchange", action="store_true",
+                    help="under torchrun: time the SP Q/K/V gather alone, encode + NCCL all_to_all "
+                         "against the peer-memory encode, and check the received bytes are equal")
     ap.add_argument("--hbm-kernels", action="store_true",
                     help="time the HBM-bound kernels at one SP rank's shapes (--sp) against the measured HBM copy bandwidth")
     ap.add_argument("--c5", choices=("auto", "on", "off"), default="auto",
@@ -726,6 +729,9 @@ def main():
     # SP degree; the tail padding rows are zeros, as split_sequence makes them).
     q, k, v = (global_rows(w, rank * s_loc, (rank + 1) * s_loc, dev)[None] for w in ("q", "k", "v"))
 
+    if args.sp_exchange:
+        return sp_exchange(args, rank, world, dev, group, q, k, v, cos, sin)
+
     backend = H3AttentionBackendB200(args.precision)
     comm_stream = torch.cuda.Stream(device=dev) if world > 1 else None
     fp8_wire = args.precision == "sage"
@@ -886,6 +892,63 @@ def main():
     del out
     if world > 1:
         dist.destroy_process_group()
+
+
+def sp_exchange(args, rank, world, dev, group, q, k, v, cos, sin):
+    """The SP layer's Q/K/V gather alone (FP8 wire, RoPE fused, one PHAA
+    chunk of all local heads): encode + NCCL all_to_all_single against the
+    peer-memory encode (xgb_fp8_wire_encode_peers + flags). CUDA events
+    around `--steps` exchanges after `--warmup`, max over ranks; the two
+    received wires are compared byte for byte first."""
+    import torch
+    import torch.distributed as dist
+
+    from xgen_b200.attention import kernel_errors
+    from xgen_b200.phaa import fp8_transport as fp8
+    from xgen_b200.phaa import peer_wire
+
+    if world < 2:
+        raise SystemExit("--sp-exchange needs torchrun with 2 or more ranks")
+    hp = HEADS // world
+    chunks = tuple(t.unflatten(-1, (world, hp, HEAD_DIM)).permute(2, 1, 0, 3, 4) for t in (q, k, v))
+
+    def nccl():
+        return fp8.fp8_exchange_wire(chunks, HEAD_DIM, group, rotary_emb=(cos, sin))[0]
+
+    def peer():
+        wire, _, _, ticket = peer_wire.exchange_wire(chunks, HEAD_DIM, group, rotary_emb=(cos, sin))
+        peer_wire.release(ticket)
+        return wire
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    a = nccl().clone()
+    b = peer().clone()
+    same = torch.tensor([int(torch.equal(a, b))], device=dev)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    res = {"sp_exchange": "qkv gather, FP8 wire with fused RoPE", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "wire_bytes_per_rank": a.numel(),
+           "remote_bytes_per_rank": a.numel() * (world - 1) // world, "bytes_equal": bool(same.item()),
+           "nccl_ms": timed(nccl), "peer_ms": timed(peer)}
+    res["nccl_ms_again"], res["peer_ms_again"] = timed(nccl), timed(peer)
+    res["errors"] = kernel_errors(dev)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    dist.barrier(device_ids=[dev.index])
+    dist.destroy_process_group()
 
 
 def block_timing(args, world, rank, dev, group, s_loc, cos, sin, comm_stream, barrier,

@@ -141,19 +141,20 @@ int xgb_fp8_wire_decode_view(const uint8_t* payload, void* const* dests, const i
                              int64_t heads, int64_t width, int64_t valid_seq,
                              int64_t peer_padding, int dtype, void* stream);
 
-/* The Q/K/V gather's encode and all-to-all in one kernel: encodes three bf16
- * [peers, seq, batch, heads] views of 128 channels (strides as
- * xgb_fp8_wire_encode_view, multiples of 8; sources 16-byte aligned) with
- * the fused rotate-half RoPE (rotary a multiple of 32, 0 for none) and
- * stores each peer's section, byte for byte as xgb_fp8_wire_encode_view with
- * peer_padding 0 writes it, at peer_dst[p] (16-byte aligned; normally
- * peer p's receive buffer at this rank's section, a peer pointer reached
- * over NVLink). peers <= 8, heads <= 12, seq*batch a multiple of 4.
- * Replaces the encode + dist.all_to_all_single pair of fp8_all_to_all_many,
- * x_base/x_base/phaa/fp8_transport.py:85-144. */
-int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t* strides, int64_t peers,
-                              int64_t seq, int64_t batch, int64_t heads, const float* cos,
-                              const float* sin, int64_t rotary, int64_t valid_seq,
+/* An SP exchange's encode and all-to-all in one kernel: encodes `streams`
+ * (1, or 3 for Q/K/V) bf16 [peers, seq, batch, heads] views of 128 channels
+ * (strides as xgb_fp8_wire_encode_view, multiples of 8; sources 16-byte
+ * aligned), with the fused rotate-half RoPE of streams 0 and 1 when streams
+ * is 3 (rotary a multiple of 32, 0 for none), and stores each peer's
+ * section, byte for byte as xgb_fp8_wire_encode_view with peer_padding 0
+ * writes it, at peer_dst[p] (16-byte aligned; normally peer p's receive
+ * buffer at this rank's section, a peer pointer reached over NVLink).
+ * peers <= 8, heads <= 12, seq*batch a multiple of 4.
+ * Replaces the encode + dist.all_to_all_single pair of fp8_all_to_all_many /
+ * fp8_all_to_all, x_base/x_base/phaa/fp8_transport.py:85-144. */
+int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t* strides, int streams,
+                              int64_t peers, int64_t seq, int64_t batch, int64_t heads,
+                              const float* cos, const float* sin, int64_t rotary, int64_t valid_seq,
                               uint8_t* const* peer_dst, void* stream);
 
 /* Store `value` into each of n (<= 64) flag words (normally in peer GPUs'

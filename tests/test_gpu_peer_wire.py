@@ -5,7 +5,9 @@ bounded epoch flags) on two GPUs:
   all_to_all_single path receives, for several exchanges in a row (both
   slots, and a slot reused after its "freed" flags), with and without the
   fused RoPE;
-- the SP attention layer over it equals the NCCL path bit for bit.
+- the returned attention output decodes to the NCCL path's values;
+- the SP attention layer over it (gather and return, 1, 2 or 4 PHAA chunks,
+  so slots are reused within a layer) equals the NCCL path bit for bit.
 
 Skips when fewer than two GPUs are visible."""
 import os
@@ -64,6 +66,15 @@ def _wire_worker(rank, world, port, results):
             torch.cuda.synchronize()
             ok.append((peers, pad) == (peers2, pad2) and torch.equal(got, expect))
             peer_wire.release(ticket)
+            # the return direction: one attention output [peers, seq, batch, heads*D]
+            out = torch.randn(world, s_loc, 1, hp * D, device=dev, generator=g).bfloat16()
+            back_nccl, back_peer = torch.empty_like(out), torch.empty_like(out)
+            fp8.fp8_all_to_all(back_nccl, out, D, dist.group.WORLD)
+            wire, peers3, _, ticket = peer_wire.exchange_wire((out.unflatten(-1, (hp, D)),), D, dist.group.WORLD)
+            fp8.decode(wire, [back_peer], D, peers3)
+            peer_wire.release(ticket)
+            torch.cuda.synchronize()
+            ok.append(torch.equal(back_peer, back_nccl))
         torch.cuda.synchronize()
         results[rank] = (ok, kernel_errors(dev))
     finally:
@@ -93,7 +104,7 @@ def _layer_worker(rank, world, port, results):
         outs = {}
         for mode in ("0", "1", "1", "0", "1"):
             os.environ["XGB_SP_PEER_WIRE"] = mode
-            for phaa in (1, 2):
+            for phaa in (1, 2, 4):
                 out = sp_self_attention(*shard, cs, backend=backend, heads=heads, head_dim=D,
                                         sp_group=dist.group.WORLD, sp_size=world, phaa_num=phaa,
                                         fp8_transport=True, comm_stream=comm_stream)

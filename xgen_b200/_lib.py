@@ -49,8 +49,8 @@ SIGNATURES = {
                                          c_i64, c_vp, c_vp]),
     "xgb_fp8_wire_decode_view": (c_int, [c_vp, ctypes.POINTER(c_vp), c_i64p, c_int, c_i64, c_i64,
                                          c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_vp]),
-    "xgb_fp8_wire_encode_peers": (c_int, [ctypes.POINTER(c_vp), c_i64p, c_i64, c_i64, c_i64, c_i64,
-                                          c_vp, c_vp, c_i64, c_i64, ctypes.POINTER(c_vp), c_vp]),
+    "xgb_fp8_wire_encode_peers": (c_int, [ctypes.POINTER(c_vp), c_i64p, c_int, c_i64, c_i64, c_i64,
+                                          c_i64, c_vp, c_vp, c_i64, c_i64, ctypes.POINTER(c_vp), c_vp]),
     "xgb_peer_signal": (c_int, [ctypes.POINTER(c_vp), c_int, c_int, c_vp]),
     "xgb_peer_wait": (c_int, [ctypes.POINTER(c_vp), c_int, c_int, c_i64, c_vp, c_vp]),
     "xgb_fp8_quantize_per_tensor_workspace": (c_i64, [c_i64]),

@@ -613,11 +613,13 @@ XGB_API int xgb_fp8_wire_decode(const uint8_t* payload, void* const* dests, int 
                                   rows, peer_padding, dtype, stream);
 }
 
-XGB_API int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t* strides, int64_t peers,
-                                      int64_t seq, int64_t batch, int64_t heads, const float* cos,
-                                      const float* sin, int64_t rotary, int64_t valid_seq,
-                                      uint8_t* const* peer_dst, void* stream) {
+XGB_API int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t* strides, int streams,
+                                      int64_t peers, int64_t seq, int64_t batch, int64_t heads,
+                                      const float* cos, const float* sin, int64_t rotary,
+                                      int64_t valid_seq, uint8_t* const* peer_dst, void* stream) {
   if (!sources || !strides || !peer_dst) return XGB_ERR_ARG;
+  if (streams != 1 && streams != 3) return XGB_ERR_ARG;
+  if (streams == 1 && rotary != 0) return XGB_ERR_ARG;  // the RoPE is for Q and K
   if (peers <= 0 || peers > kMaxPeers || seq <= 0 || batch <= 0 || heads <= 0) return XGB_ERR_SHAPE;
   if (valid_seq <= 0 || valid_seq > peers * seq) return XGB_ERR_SHAPE;
   // whole warps of 4 positions inside one peer; shared-memory span per warp
@@ -629,7 +631,7 @@ XGB_API int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t*
   EncodeArgs a{};
   a.rows = peers * seq * batch * heads;
   if (a.rows > INT32_MAX) return XGB_ERR_SHAPE;
-  for (int s = 0; s < 3; ++s) {
+  for (int s = 0; s < streams; ++s) {
     if (!sources[s]) return XGB_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(sources[s]) & 15u) return XGB_ERR_ALIGN;
     a.src[s] = sources[s];
@@ -646,7 +648,7 @@ XGB_API int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t*
   }
   a.peers = peers; a.seq = seq; a.batch = batch; a.heads = heads; a.width = 128;
   a.peer_rows = a.rows / peers;
-  a.peer_padding = 0; a.streams = 3; a.valid_seq = valid_seq;
+  a.peer_padding = 0; a.streams = streams; a.valid_seq = valid_seq;
   a.div_heads = make_fastdiv(static_cast<uint32_t>(heads));
   a.div_batch = make_fastdiv(static_cast<uint32_t>(batch));
   a.div_seq = make_fastdiv(static_cast<uint32_t>(seq));
@@ -657,7 +659,7 @@ XGB_API int xgb_fp8_wire_encode_peers(const void* const* sources, const int64_t*
           cudaSuccess)
     return XGB_ERR_LAUNCH;
   const int64_t positions = a.rows / heads;
-  const dim3 grid(static_cast<unsigned>(cdiv(positions, (kThreads / 32) * kPeerPositions)), 3);
+  const dim3 grid(static_cast<unsigned>(cdiv(positions, (kThreads / 32) * kPeerPositions)), streams);
   wire_encode_peers_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(a, pd);
   return launch_status();
 }

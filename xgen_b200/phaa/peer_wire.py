@@ -1,11 +1,13 @@
-"""The SP Q/K/V gather as one kernel over NVLink (B200 extension of PHAA).
+"""The SP exchanges as one kernel each over NVLink (B200 extension of PHAA).
 
-`fp8_transport.fp8_exchange_wire` encodes Q/K/V into a local send buffer and
-moves it with NCCL `all_to_all_single` (x_base/x_base/phaa/fp8_transport.py
+`fp8_transport.fp8_exchange_wire` / `fp8_all_to_all` encode Q/K/V (the
+gather) or the attention output (the return) into a local send buffer and
+move it with NCCL `all_to_all_single` (x_base/x_base/phaa/fp8_transport.py
 :85-144). Here the encode kernel (`xgb_fp8_wire_encode_peers`) stores each
 peer's rows straight into that peer's receive buffer, at the offset the
 all-to-all would have delivered them to, so the received wire is byte for
-byte the NCCL path's and `sage_prepare_wire` reads it unchanged.
+byte the NCCL path's: `sage_prepare_wire` reads the gathered one unchanged
+and the wire decode reads the returned one.
 
 The receive buffers live in symmetric memory (`torch.distributed.
 _symmetric_memory`: every rank maps every other rank's buffer), two slots
@@ -19,8 +21,9 @@ by epoch flags at the end of the buffers, all waits bounded:
      flag in this rank's buffer reaches e,
   4. the consumer reads the slot; `release` then signals "freed" = e.
 
-A rank never waits on its own flags: its own section is ordered by its
-streams (the comm stream waits for the compute stream at each layer).
+A rank never waits on its own flags: its own section of a slot is ordered
+by a CUDA event that `release` records on the reading stream and the next
+exchange into that slot waits for on its own stream.
 """
 from __future__ import annotations
 
@@ -41,14 +44,17 @@ _wires: dict = {}
 
 
 def enabled() -> bool:
-    """XGB_SP_PEER_WIRE=1 routes eligible Sage gathers through this path."""
+    """XGB_SP_PEER_WIRE=1 routes the eligible FP8-wire exchanges of PHAA (the
+    Sage gather read straight from the wire, and the return) through this
+    path."""
     return os.environ.get("XGB_SP_PEER_WIRE", "0") == "1"
 
 
 def eligible(tensors, head_dim: int, group) -> bool:
-    """Q/K/V chunk views [peers, seq, batch, heads, 128] in bf16 on the GPU,
-    at most 8 peers and 12 heads per peer, seq*batch a multiple of 4."""
-    if len(tensors) != 3 or head_dim != 128 or group is None:
+    """Q/K/V chunk views, or one returned attention output, [peers, seq,
+    batch, heads, 128] in bf16 on the GPU, at most 8 peers and 12 heads per
+    peer, seq*batch a multiple of 4."""
+    if len(tensors) not in (1, 3) or head_dim != 128 or group is None:
         return False
     t = tensors[0]
     if t.ndim != 5 or not t.is_cuda or any(x.dtype != torch.bfloat16 or x.shape != t.shape for x in tensors):
@@ -85,6 +91,7 @@ class PeerWire:
         self.handle = symm_mem.rendezvous(self.buf, group)
         self.ptrs = [int(p) for p in self.handle.buffer_ptrs]
         self.others = [p for p in range(self.peers) if p != self.rank]
+        self.freed = [None, None]  # per slot: event after this rank's own reads
         self.epoch = 0
 
     def _flag(self, owner: int, kind: int, slot: int, src: int) -> int:
@@ -99,7 +106,7 @@ class PeerWire:
         call("xgb_peer_signal", ptr_array(flags), len(flags), value, stream)
 
     def exchange(self, tensors, rotary_emb=None, valid_seq: int | None = None):
-        """Encode Q/K/V views [peers, seq, batch, heads, 128] into every
+        """Encode 1 or 3 views [peers, seq, batch, heads, 128] into every
         peer's next slot; returns (received wire uint8 [slot_bytes], ticket)
         on the current stream."""
         from ..attention import _err_flag
@@ -109,6 +116,8 @@ class PeerWire:
         err = _err_flag(device).data_ptr()
         e = self.epoch + 1
         slot = e % 2
+        if self.freed[slot] is not None:
+            torch.cuda.current_stream(device).wait_event(self.freed[slot])
         if e > 2:
             self._wait(_FREED, slot, e - 2, stream, err)
         views = [WireView.of(t) for t in tensors]
@@ -120,7 +129,7 @@ class PeerWire:
             cos, sin = rotary_emb
             rotary = cos.shape[-1]
         call("xgb_fp8_wire_encode_peers", ptr_array(v.ptr for v in views),
-             i64_array(s for v in views for s in v.strides), peers, seq, batch, heads,
+             i64_array(s for v in views for s in v.strides), len(views), peers, seq, batch, heads,
              cos.data_ptr() if cos is not None else None, sin.data_ptr() if sin is not None else None,
              rotary, peers * seq if valid_seq is None else valid_seq, ptr_array(dst), stream)
         self._signal(_ARRIVED, slot, e, stream)
@@ -136,8 +145,8 @@ def exchange_wire(tensors, head_dim: int, group, *, rotary_emb=None):
     that reads the wire, after its reads."""
     rows = [_rows_view(t, dist.get_world_size(group), head_dim) for t in tensors]
     peers, seq, batch, heads, _ = rows[0].shape
-    slot_bytes = peers * 3 * seq * batch * heads * _ROW_BYTES
-    key = (dist.get_rank(), id(group), slot_bytes, tensors[0].device.index)
+    slot_bytes = peers * len(rows) * seq * batch * heads * _ROW_BYTES
+    key = (id(group), len(rows), slot_bytes, tensors[0].device.index)
     pw = _wires.get(key)
     if pw is None:
         pw = _wires[key] = PeerWire(group, slot_bytes, tensors[0].device)
@@ -148,5 +157,8 @@ def exchange_wire(tensors, head_dim: int, group, *, rotary_emb=None):
 def release(ticket) -> None:
     """Tell every peer this rank has finished reading the ticket's slot."""
     pw, e, slot = ticket
-    stream = torch.cuda.current_stream(pw.buf.device).cuda_stream
-    pw._signal(_FREED, slot, e, stream)
+    cur = torch.cuda.current_stream(pw.buf.device)
+    pw._signal(_FREED, slot, e, cur.cuda_stream)
+    ev = torch.cuda.Event()
+    ev.record(cur)
+    pw.freed[slot] = ev

@@ -258,6 +258,13 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
                         None if direct_return else (returned[step],), (results[step],), D,
                         output_group, row_tiling=async_options.row_tiling,
                         return_shard_seq=Sq if fused_return_pack else 0))
+                elif (fp8_transport and peer_wire.enabled() and
+                      peer_wire.eligible((results[step].unflatten(-1, (-1, D)),), D, output_group)):
+                    # B200: encode the output straight into the peers' receive buffers
+                    wire, peers, _, ticket = peer_wire.exchange_wire(
+                        (results[step].unflatten(-1, (-1, D)),), D, output_group)
+                    fp8.decode(wire, [returned[step]], D, peers)
+                    peer_wire.release(ticket)
                 else:
                     exchange_one(returned[step], results[step], output_group)
                 if device_join:
