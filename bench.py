@@ -699,6 +699,8 @@ def main():
     os.environ["XGB_SP_PEER_WIRE"] = "1" if args.wire_transport == "peer" else "0"
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    all_cpus = os.sched_getaffinity(0)
+    host_cpus = bind_host_to_gpu(dev)
     group = None
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
@@ -806,9 +808,11 @@ def main():
     e2e = None
     if not args.no_e2e:
         e2e = end_to_end(step, q, k, v, args, world, dev, barrier, max_over_ranks)
+        e2e["host_cpus_per_rank"] = host_cpus  # GPU-local CPUs the rank ran on (None: not bound)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core it may
         tflops, flops, secs, used = cpu_attention_sample(args.cpu_seconds)
         cpu = {"value": tflops, "unit": "TFLOP/s", "cores": used, "kind": "port",
                "sample": f"fp32 SDPA (oracle port of attention.py:29-34) on 1 head: "
@@ -1177,12 +1181,42 @@ def profile_traffic(precision, heads):
     return rec["dram_bytes_per_head"] * heads
 
 
+def bind_host_to_gpu(dev):
+    """Restrict this rank's host threads to the CPUs NVML lists as local to
+    its GPU (intersected with the CPUs the process may use), before any
+    pinned host buffer exists, so the e2e staging buffers are allocated on the
+    GPU's own NUMA node. Process placement only: no GPU setting is read or
+    changed beyond the affinity query. Returns the number of CPUs kept, or
+    None when NVML gives no usable answer."""
+    import torch
+
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(dev).uuid)
+            handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, max(1, (os.cpu_count() or 64) // 64 + 1))
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:  # noqa: BLE001 - no NVML or no answer: leave placement to the OS
+        return None
+    local = {w * 64 + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+    keep = local & os.sched_getaffinity(0)
+    if not keep:
+        return None
+    os.sched_setaffinity(0, keep)
+    return len(keep)
+
+
 def end_to_end(step, q, k, v, args, world, dev, barrier, max_over_ranks):
     """Same layer through the public API with pinned host buffers: every
     step's Q/K/V shard is copied host->device and its output device->host
-    inside the timed region. The copies run on a side stream with two device
-    buffer sets, so step i+1's upload and step i-1's download overlap step
-    i's compute (the way a serving loop would feed the layer)."""
+    inside the timed region. Uploads and downloads run on two side streams
+    (one per copy direction, so they proceed at once) with two device buffer
+    sets, so step i+1's upload and step i-1's download overlap step i's
+    compute (the way a serving loop would feed the layer)."""
     import torch
 
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
@@ -1192,17 +1226,18 @@ def end_to_end(step, q, k, v, args, world, dev, barrier, max_over_ranks):
     steps = max(2, min(args.steps, 20))
     bufs = [tuple(torch.empty_like(t) for t in (q, k, v)) for _ in range(2)]
     cs = torch.cuda.current_stream(dev)
-    xs = torch.cuda.Stream(device=dev)
+    up = torch.cuda.Stream(device=dev)    # host -> device
+    down = torch.cuda.Stream(device=dev)  # device -> host
     loaded = [torch.cuda.Event() for _ in range(2)]
     computed = [torch.cuda.Event() for _ in range(2)]
 
     def upload(i):
-        with torch.cuda.stream(xs):
+        with torch.cuda.stream(up):
             if i >= 2:
-                xs.wait_event(computed[i % 2])  # step i-2 has finished reading this set
+                up.wait_event(computed[i % 2])  # step i-2 has finished reading this set
             for d, h in zip(bufs[i % 2], (hq, hk, hv)):
                 d.copy_(h, non_blocking=True)
-            loaded[i % 2].record(xs)
+            loaded[i % 2].record(up)
 
     def run(n):
         upload(0)
@@ -1212,17 +1247,19 @@ def end_to_end(step, q, k, v, args, world, dev, barrier, max_over_ranks):
             cs.wait_event(loaded[i % 2])
             out = step(*bufs[i % 2])
             computed[i % 2].record(cs)
-            with torch.cuda.stream(xs):
-                xs.wait_event(computed[i % 2])
+            with torch.cuda.stream(down):
+                down.wait_event(computed[i % 2])
                 houts[i % 2].copy_(out, non_blocking=True)
-                out.record_stream(xs)
-        cs.wait_stream(xs)
+                out.record_stream(down)
+        cs.wait_stream(up)
+        cs.wait_stream(down)
 
     run(2)
     barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record(cs)
-    xs.wait_event(s)
+    up.wait_event(s)
+    down.wait_event(s)
     run(steps)
     e.record(cs)
     barrier()

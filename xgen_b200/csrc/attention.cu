@@ -87,6 +87,40 @@ constexpr bool kTurn = XGB_ATTN_TURN != 0;
 constexpr bool kInitMma = XGB_ATTN_INIT_MMA != 0;
 constexpr uint32_t kInitAWord = 0x66666666u;  // e5m2 1536 in every byte
 constexpr uint32_t kInitBWord = 0x5C5C5C5Cu;  // e5m2 256 in every byte
+// Order of the Sage exp section: 0 works through the keys four at a time
+// (arguments, exponentials, sums and packing of each group together); 1
+// forms every argument of the tile, then every exponential, then the sums
+// and packing.
+#ifndef XGB_ATTN_EXP_ORDER
+#define XGB_ATTN_EXP_ORDER 1
+#endif
+constexpr int kExpOrder = XGB_ATTN_EXP_ORDER;
+// Packing of four e4m3 P values into one TMEM word: 0 joins the two
+// converted pairs by shift and or; 1 by one 32-bit move of the two 16-bit
+// halves.
+#ifndef XGB_ATTN_PACK
+#define XGB_ATTN_PACK 1
+#endif
+__device__ __forceinline__ uint32_t pack_p4(float a, float b, float c, float d) {
+  if constexpr (XGB_ATTN_PACK == 1) {
+    uint32_t w;
+    asm("{\n\t.reg .b16 lo, hi;\n\t"
+        "cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n\t"
+        "cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n\t"
+        "mov.b32 %0, {lo, hi};\n\t}"
+        : "=r"(w)
+        : "f"(a), "f"(b), "f"(c), "f"(d));
+    return w;
+  } else {
+    return pack_e4m3x2(a, b) | (pack_e4m3x2(c, d) << 16);
+  }
+}
+// Row sums: 0 adds each tile's partial sums to the row's total; 1 keeps the
+// partials running across tiles (rescaled with O) and sums them at the end.
+#ifndef XGB_ATTN_LSUM
+#define XGB_ATTN_LSUM 1
+#endif
+constexpr bool kLsum = XGB_ATTN_LSUM != 0;
 constexpr int kTurnBar = 1;  // named barriers 1, 2: exp turn of WG0, WG1
 constexpr int kEpiBar = 3;   // named barrier 3: the 256 softmax threads in the split epilogue
 constexpr uint32_t kMagic = 0x4B400000u;
@@ -371,6 +405,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     float m_used = kNegInf;
     float l = 0.f;
+    // Row-sum partials (four packed chains). kLsum: they run across the tiles
+    // and are summed once after the loop; otherwise each tile's are added to l.
+    float rsa[4] = {0.f, 0.f, 0.f, 0.f}, rsb[4] = {0.f, 0.f, 0.f, 0.f};
     float ks = 0.f;  // K-block scale of the current tile (Sage)
     if constexpr (kSage && !kWire) ks = p.k_scale[static_cast<int64_t>(bh) * p.scale_stride + kv0];
     // Wire layout: the four 16-key group scales of the current and next tile
@@ -483,7 +520,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float alpha = need ? ex2_approx(m_used - m_new) : 1.0f;
         if (need) m_used = m_new;
-        l *= alpha;
+        if constexpr (kLsum) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            rsa[j] *= alpha;
+            rsb[j] *= alpha;
+          }
+        } else {
+          l *= alpha;
+        }
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -499,7 +544,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = exp2(comb*s - m_used) (times kPScale for e4m3, folded into the
       // exponent), row sum, pack and store over the S buffer.
       // Row sums in four independent packed chains (short dependency chains).
-      float rsa[4] = {0.f, 0.f, 0.f, 0.f}, rsb[4] = {0.f, 0.f, 0.f, 0.f};
+      if constexpr (!kLsum) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) rsa[j] = rsb[j] = 0.f;
+      }
       if constexpr (kSage) {
         const float off = (kLog2PScale - m_used) - 12582912.0f * comb;
         float offs[4];
@@ -508,6 +556,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 4; ++j) offs[j] = (kLog2PScale - m_used) - 12582912.0f * comb4[j];
         }
         uint32_t packed[16];  // 64 keys of e4m3 P = 16 TMEM columns
+        if constexpr (kExpOrder == 1 && !kWire) {
+          // every argument, then every exponential, then sums and packing
+          float pv[2][32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2)
+              ffma2(pv[c][e], pv[c][e + 1], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), comb, comb,
+                    off, off);
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              if (poly_pair((c * 32 + e) / 2)) {
+                ex2_poly2<2>(pv[c][e], pv[c][e + 1], pv[c][e], pv[c][e + 1]);
+              } else {
+                pv[c][e] = ex2_approx(pv[c][e]);
+                pv[c][e + 1] = ex2_approx(pv[c][e + 1]);
+              }
+            }
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const int ch = (e / 4) & 1;
+              fadd2(rsa[2 * ch], rsb[2 * ch], rsa[2 * ch], rsb[2 * ch], pv[c][e], pv[c][e + 1]);
+              fadd2(rsa[2 * ch + 1], rsb[2 * ch + 1], rsa[2 * ch + 1], rsb[2 * ch + 1], pv[c][e + 2], pv[c][e + 3]);
+              packed[c * 8 + e / 4] = pack_p4(pv[c][e], pv[c][e + 1], pv[c][e + 2], pv[c][e + 3]);
+            }
+        } else
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
 #pragma unroll
@@ -529,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ch = (e / 4) & 1;
             fadd2(rsa[2 * ch], rsb[2 * ch], rsa[2 * ch], rsb[2 * ch], pv[0], pv[1]);
             fadd2(rsa[2 * ch + 1], rsb[2 * ch + 1], rsa[2 * ch + 1], rsb[2 * ch + 1], pv[2], pv[3]);
-            packed[c * 8 + e / 4] = pack_e4m3x2(pv[0], pv[1]) | (pack_e4m3x2(pv[2], pv[3]) << 16);
+            packed[c * 8 + e / 4] = pack_p4(pv[0], pv[1], pv[2], pv[3]);
           }
         }
         tmem_st16(s_addr, packed);
@@ -555,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(i == 1 && t == n_kv - 1)) named_arrive(turn_other, 2 * kBM);
         turns = t + 1;
       }
-      l += ((rsa[0] + rsb[0]) + (rsa[1] + rsb[1])) + ((rsa[2] + rsb[2]) + (rsa[3] + rsb[3]));
+      if constexpr (!kLsum) l += ((rsa[0] + rsb[0]) + (rsa[1] + rsb[1])) + ((rsa[2] + rsb[2]) + (rsa[3] + rsb[3]));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->p_full[i][t & 1]);
@@ -566,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(i == 1 && t == n_kv - 1)) named_arrive(turn_other, 2 * kBM);
       }
     }
+    if constexpr (kLsum) l = ((rsa[0] + rsb[0]) + (rsa[1] + rsb[1])) + ((rsa[2] + rsb[2]) + (rsa[3] + rsb[3]));
     // ------------------------------------------------------------ epilogue
     // pv_done may trail the last tile by two phases here, so a parity wait
     // on it would be ambiguous; o_done completes exactly once.
