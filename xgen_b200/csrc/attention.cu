@@ -121,6 +121,11 @@ __device__ __forceinline__ uint32_t pack_p4(float a, float b, float c, float d) 
 #define XGB_ATTN_LSUM 1
 #endif
 constexpr bool kLsum = XGB_ATTN_LSUM != 0;
+// S tile read from TMEM as one 64-column load (1) or two of 32 columns (0).
+#ifndef XGB_ATTN_LD64
+#define XGB_ATTN_LD64 1
+#endif
+constexpr bool kLd64 = XGB_ATTN_LD64 != 0;
 constexpr int kTurnBar = 1;  // named barriers 1, 2: exp turn of WG0, WG1
 constexpr int kEpiBar = 3;   // named barrier 3: the 256 softmax threads in the split epilogue
 constexpr uint32_t kMagic = 0x4B400000u;
@@ -442,8 +447,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       uint32_t r[2][32];
-      tmem_ld32(s_addr, r[0]);
-      tmem_ld32(s_addr + 32, r[1]);
+      if constexpr (kLd64) {
+        tmem_ld64(s_addr, r);
+      } else {
+        tmem_ld32(s_addr, r[0]);
+        tmem_ld32(s_addr + 32, r[1]);
+      }
       tmem_ld_wait();
       // Sage: the int32 scores s are read as the exact floats 12582912 + s:
       // their accumulator started at the bits 0x4B400000 (kInit), or the
