@@ -155,8 +155,17 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
         final = torch.empty((B, Sq, H), device=query.device, dtype=query.dtype)
         returned = None
     else:
+        # The layer's output [B, Sq, H]: head peer*hpd + offsets[i] + j of
+        # chunk i. The peer return decodes straight into it; the other paths
+        # receive into `returned` and are copied in at the end.
+        final = torch.empty((B, Sq, H), device=query.device, dtype=query.dtype)
         returned = [torch.empty((W_S, Sq, B, cs * D), device=query.device, dtype=query.dtype)
                     for cs in sizes]
+    decoded_in_place = set()
+
+    def final_chunk(i):
+        """Chunk i's heads of `final` as a [W_S, Sq, B, cs, D] view."""
+        return final.view(B, Sq, W_S, hpd, D).narrow(3, offsets[i], sizes[i]).permute(2, 1, 0, 3, 4)
     pending_gathers, pending_returns = {}, []
     if async_exchange:
         from .fp8_async_transport import finish_fp8_exchange, submit_fp8_exchange
@@ -260,10 +269,12 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
                         return_shard_seq=Sq if fused_return_pack else 0))
                 elif (fp8_transport and peer_wire.enabled() and
                       peer_wire.eligible((results[step].unflatten(-1, (-1, D)),), D, output_group)):
-                    # B200: encode the output straight into the peers' receive buffers
+                    # B200: encode the output straight into the peers' receive buffers,
+                    # then decode it into the layer's output in place
                     wire, peers, _, ticket = peer_wire.exchange_wire(
                         (results[step].unflatten(-1, (-1, D)),), D, output_group)
-                    fp8.decode(wire, [returned[step]], D, peers)
+                    fp8.decode_view(wire, [fp8.WireView.of(final_chunk(step))], D)
+                    decoded_in_place.add(step)
                     peer_wire.release(ticket)
                 else:
                     exchange_one(returned[step], results[step], output_group)
@@ -287,7 +298,10 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
         scatter_stream.synchronize()
     if direct_return:
         return final
-    return torch.cat([b.permute(2, 1, 0, 3) for b in returned], dim=3).flatten(-2, -1)
+    for i, b in enumerate(returned):
+        if i not in decoded_in_place:
+            final_chunk(i).copy_(b.unflatten(-1, (sizes[i], D)))
+    return final
 
 
 def _int8_wire(query, key, value, *, comm_stream, sp_group, sp_size, heads, phaa_split_num,
