@@ -83,6 +83,9 @@ def parse():
                          "against the peer-memory encode, and check the received bytes are equal")
     ap.add_argument("--hbm-kernels", action="store_true",
                     help="time the HBM-bound kernels at one SP rank's shapes (--sp) against the measured HBM copy bandwidth")
+    ap.add_argument("--timeline", action="store_true",
+                    help="print a CUDA-event timeline of the SP layer's stages (gather, preparation, "
+                         "attention, return, decode) instead of the bench line")
     ap.add_argument("--c5", choices=("auto", "on", "off"), default="auto",
                     help="BASELINE config 5 (two blocks at 768P-15s, 20 steps): auto = at 8 GPUs only")
     return ap.parse_args()
@@ -761,6 +764,8 @@ def main():
     for _ in range(args.warmup):
         out = step(q, k, v)
     barrier()
+    if args.timeline:
+        return layer_timeline(args, step, q, k, v, rank, world, dev, barrier, max_over_ranks)
     launches_before = backend.kernel_calls
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -1179,6 +1184,43 @@ def profile_traffic(precision, heads):
         return None
     rec = json.loads(path.read_text())
     return rec["dram_bytes_per_head"] * heads
+
+
+def layer_timeline(args, step, q, k, v, rank, world, dev, barrier, max_over_ranks):
+    """--timeline: `--steps` layers, each with a CUDA-event timeline of its
+    stages (xgen_b200.trace); per stage the mean milliseconds it added to a
+    layer, max over ranks, next to the layer's own time."""
+    import torch
+
+    import torch.distributed as dist
+
+    from xgen_b200 import trace
+
+    if world < 2 or args.precision != "sage" or args.wire != "fp8":
+        raise SystemExit("--timeline covers the Sage FP8-wire SP layer: torchrun with 2 or more ranks")
+    totals: dict = {}
+    layer_ms = 0.0
+    for _ in range(args.steps):
+        barrier()
+        trace.start()
+        out = step(q, k, v)
+        events = trace.stop()
+        torch.cuda.synchronize()
+        for name, ms in trace.stage_ms(events).items():
+            totals[name] = totals.get(name, 0.0) + ms
+        layer_ms += events[0][1].elapsed_time(events[-1][1])
+        del out
+    stages = {name: max_over_ranks(ms / args.steps) for name, ms in totals.items()}
+    res = {"timeline": "SP self-attention layer at 768P-5s", "n_gpus": world, "steps": args.steps,
+           "precision": args.precision, "wire_transport": args.wire_transport,
+           "layer_ms": max_over_ranks(layer_ms / args.steps), "stage_ms": stages,
+           "stages": "gathered: encode + exchange of Q/K/V until every peer's rows arrived; prepared: Sage "
+                     "preparation from the wire; attended: attention kernel; returned: encode + exchange "
+                     "of the output; decoded: decode into the layer output; end: the compute stream's join"}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    barrier()
+    dist.destroy_process_group()
 
 
 def bind_host_to_gpu(dev):

@@ -18,7 +18,7 @@ import os
 import torch
 import torch.nn.functional as F
 
-from . import _lib
+from . import _lib, trace
 from ._lib import call, i64_array
 
 HEAD_DIM = 128
@@ -235,7 +235,9 @@ class H3AttentionBackendB200:
         ws = sage_prepare_wire(wire, peers=peers, seq=seq, batch=batch, heads=heads, valid_seq=valid_seq,
                                peer_padding=peer_padding, ws=self._ws.get(key_))
         self._ws[key_] = ws
+        trace.mark("prepared")
         sage_attention_prepared(ws, out)
+        trace.mark("attended")
         self.kernel_calls += 1
         self.calls += 1
         return out

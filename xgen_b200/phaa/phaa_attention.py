@@ -32,6 +32,7 @@ import torch
 import torch.distributed as dist
 
 from ..sp.padding import get_pad_manager
+from .. import trace
 from . import fp8_transport as fp8
 from . import peer_wire
 
@@ -196,12 +197,14 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
                 exchange_one(out, inp, sp_group)
         gathered[i].record(comm_stream)
 
+    trace.mark("start")
     comm_stream.wait_stream(acc.current_stream())
     if scatter_stream is not None:
         scatter_stream.wait_stream(acc.current_stream())
     with acc.stream(comm_stream):
         for i in (order if gather_priority else order[:1]):
             gather_chunk(i)
+            trace.mark("gathered", comm_stream)
 
     for pos, step in enumerate(order):
         if async_exchange:
@@ -273,7 +276,9 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
                     # then decode it into the layer's output in place
                     wire, peers, _, ticket = peer_wire.exchange_wire(
                         (results[step].unflatten(-1, (-1, D)),), D, output_group)
+                    trace.mark("returned", comm_stream)
                     fp8.decode_view(wire, [fp8.WireView.of(final_chunk(step))], D)
+                    trace.mark("decoded", comm_stream)
                     decoded_in_place.add(step)
                     peer_wire.release(ticket)
                 else:
@@ -296,6 +301,7 @@ def run_phaa_attention(query, key, value, *, comm_stream, sp_group, sp_size, hea
         comm_stream.synchronize()
     if scatter_stream is not None:
         scatter_stream.synchronize()
+    trace.mark("end")
     if direct_return:
         return final
     for i, b in enumerate(returned):
