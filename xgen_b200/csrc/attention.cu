@@ -594,29 +594,30 @@ __global__ void __launch_bounds__(kThreads, 1)
               fadd2(rsa[2 * ch + 1], rsb[2 * ch + 1], rsa[2 * ch + 1], rsb[2 * ch + 1], pv[c][e + 2], pv[c][e + 3]);
               packed[c * 8 + e / 4] = pack_p4(pv[c][e], pv[c][e + 1], pv[c][e + 2], pv[c][e + 3]);
             }
-        } else
+        } else {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < 2; ++c) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float x[4], pv[4];
-            const float cb = kWire ? comb4[c * 2 + e / 16] : comb;
-            const float of = kWire ? offs[c * 2 + e / 16] : off;
-            ffma2(x[0], x[1], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), cb, cb, of, of);
-            ffma2(x[2], x[3], __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]), cb, cb, of, of);
+            for (int e = 0; e < 32; e += 4) {
+              float x[4], pv[4];
+              const float cb = kWire ? comb4[c * 2 + e / 16] : comb;
+              const float of = kWire ? offs[c * 2 + e / 16] : off;
+              ffma2(x[0], x[1], __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]), cb, cb, of, of);
+              ffma2(x[2], x[3], __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]), cb, cb, of, of);
 #pragma unroll
-            for (int u = 0; u < 4; u += 2) {
-              if (poly_pair((c * 32 + e + u) / 2)) {
-                ex2_poly2<2>(pv[u], pv[u + 1], x[u], x[u + 1]);
-              } else {
-                pv[u] = ex2_approx(x[u]);
-                pv[u + 1] = ex2_approx(x[u + 1]);
+              for (int u = 0; u < 4; u += 2) {
+                if (poly_pair((c * 32 + e + u) / 2)) {
+                  ex2_poly2<2>(pv[u], pv[u + 1], x[u], x[u + 1]);
+                } else {
+                  pv[u] = ex2_approx(x[u]);
+                  pv[u + 1] = ex2_approx(x[u + 1]);
+                }
               }
+              const int ch = (e / 4) & 1;
+              fadd2(rsa[2 * ch], rsb[2 * ch], rsa[2 * ch], rsb[2 * ch], pv[0], pv[1]);
+              fadd2(rsa[2 * ch + 1], rsb[2 * ch + 1], rsa[2 * ch + 1], rsb[2 * ch + 1], pv[2], pv[3]);
+              packed[c * 8 + e / 4] = pack_p4(pv[0], pv[1], pv[2], pv[3]);
             }
-            const int ch = (e / 4) & 1;
-            fadd2(rsa[2 * ch], rsb[2 * ch], rsa[2 * ch], rsb[2 * ch], pv[0], pv[1]);
-            fadd2(rsa[2 * ch + 1], rsb[2 * ch + 1], rsa[2 * ch + 1], rsb[2 * ch + 1], pv[2], pv[3]);
-            packed[c * 8 + e / 4] = pack_p4(pv[0], pv[1], pv[2], pv[3]);
           }
         }
         tmem_st16(s_addr, packed);
