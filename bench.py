@@ -655,7 +655,9 @@ def run_reference(args):
         "ms_per_step": FLOPS_PER_LAYER / (value * 1e12) * 1e3,
         "ms_per_step_basis": "extrapolated: one 24-head layer at the rate the 1-head sample measured",
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": workload_config(world, "reference-cpu"),
+        "data": "synthetic", "config": workload_config(world, args.precision, args.wire),
+        "reference_path": "the reference's CPU attention path (fp32 SDPA, x_base/x_base/operator/attention.py:29-34) "
+                          "on the same workload; it has no Sage or FP8 arithmetic",
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": used, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
