@@ -85,3 +85,39 @@ def test_launch_accounting():
     assert bench.kernels_per_step("sage", 1, 1, "fp8", "peer") == 2
     assert bench.kernels_per_step("sage", 2, 1, "int8") == 6
     assert bench.kernels_per_step("bf16", 4, 2) == 3
+
+
+def test_reference_arm_reports_the_b200_arm_config(monkeypatch, capsys):
+    """The reference arm's JSON line carries the same workload config as the
+    B200 arm's (the driver compares the two lines), with its CPU path named
+    on its own key."""
+    monkeypatch.setattr(bench, "cpu_attention_sample", lambda seconds, threads=None: (2.0, 1.0, 0.5, 4))
+    monkeypatch.delenv("RANK", raising=False)
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    monkeypatch.setattr("sys.argv", ["bench.py", "--impl", "reference", "--steps", "2", "--warmup", "1"])
+    bench.main()
+    import json
+
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    assert line["config"] == bench.workload_config(1, "sage", "fp8")
+    assert "reference_path" in line and line["value"] == 2.0
+
+
+def test_trace_stage_times_are_differences_of_consecutive_marks():
+    """xgen_b200.trace: each stage's time is the gap from the previous mark;
+    repeated names add up; with no timeline open, mark() records nothing."""
+    from xgen_b200 import trace
+
+    class Ev:
+        def __init__(self, t):
+            self.t = t
+
+        def elapsed_time(self, other):
+            return other.t - self.t
+
+    events = [("start", Ev(0.0)), ("gathered", Ev(1.5)), ("attended", Ev(11.5)), ("gathered", Ev(12.0))]
+    assert trace.stage_ms(events) == {"gathered": 2.0, "attended": 10.0}
+    assert trace.stop() == []
+    trace.mark("start")  # no timeline open: no CUDA call, nothing kept
+    assert trace.stop() == []
